@@ -1,0 +1,508 @@
+#!/usr/bin/env python
+"""Benchmark of the paged-KV decode hot path on B200 (one JSON line on stdout).
+
+Workload ("long ragged decode with split-KV"): per GPU a
+batch of 64 requests with context lengths drawn uniformly from [1, 8192]
+(seeded), 32 query heads, 8 KV heads, head_dim 128, block_size 16, bfloat16,
+physical pool = total blocks + 10 %, shuffled allocation.  One *step* is one
+decode step of the hot path for the batch:
+
+  1. append the new token's K/V of every request through its slot
+     (``append_kv``, reshape-and-cache), then
+  2. paged decode attention of every request over its whole context
+     (``paged_decode_attention``), context length = drawn length.
+
+The step is idempotent (the same slots are rewritten), so K timed steps are
+K identical passes over a 1.08 GB working set -- far larger than the 126 MB
+L2, so no flush is needed between steps.
+
+``value`` = algorithmic bytes of a step (K/V + Q + O + block table + lengths of
+the attention, plus the append's read and write) x steps x GPUs / the max over
+ranks of the device time of the K steps.  ``e2e`` repeats the measurement
+through the same public API with every step's inputs copied from pinned host
+memory and the output copied back inside the timed region.  ``roofline`` is the
+decode kernel alone, timed with CUDA events around each of its launches.
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+numpy restatement in ``oracle/`` of the reference's ``paged_decode_attention``)
+on a bounded sample of the same workload, with all host threads.
+
+Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): every rank owns
+its own 64-request batch and its own block pool (requests are partitioned by
+rank, weak scaling); there is no collective on the data path.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "paged-decode-attn achieved HBM GB/s"
+WORKLOAD = ("config3: ragged paged decode step, B=64/GPU, ctx~U[1,8192], Hq32/Hkv8, D128, "
+            "BS16, bf16, pool=1.1x shuffled, 1-token KV append + split-KV attention")
+
+
+# --------------------------------------------------------------- workload
+
+class Workload:
+    def __init__(self, seed: int, device: torch.device, batch=64, num_heads=32, num_kv_heads=8,
+                 head_dim=128, block_size=16, max_ctx=8192, dtype=torch.bfloat16):
+        from inferkernellab_b200 import PagedKVCache
+
+        self.batch, self.num_heads, self.num_kv_heads = batch, num_heads, num_kv_heads
+        self.head_dim, self.block_size, self.dtype = head_dim, block_size, dtype
+        lens = torch.tensor(workload_lens(seed, batch, max_ctx))
+        gen = torch.Generator().manual_seed(seed + 7)
+        need = (lens + block_size - 1) // block_size
+        num_blocks = int(math.ceil(1.1 * int(need.sum())))
+        perm = torch.randperm(num_blocks, generator=gen)
+        width = int(need.max())
+        tables = torch.zeros(batch, width, dtype=torch.int32)
+        cursor = 0
+        for b in range(batch):
+            n = int(need[b])
+            tables[b, :n] = perm[cursor:cursor + n].to(torch.int32)
+            cursor += n
+        self.lens_list = lens.tolist()
+        self.tables_host = tables
+        self.cache = PagedKVCache(num_blocks, block_size, num_kv_heads, head_dim, dtype=dtype,
+                                  device=device)
+        dgen = torch.Generator(device=device).manual_seed(seed + 1)
+        self.cache.k.copy_(torch.randn(self.cache.k.shape, generator=dgen, device=device, dtype=dtype))
+        self.cache.v.copy_(torch.randn(self.cache.v.shape, generator=dgen, device=device, dtype=dtype))
+        self.query = torch.randn(batch, num_heads, head_dim, generator=dgen, device=device, dtype=dtype)
+        self.new_k = torch.randn(batch, num_kv_heads, head_dim, generator=dgen, device=device,
+                                 dtype=dtype)
+        self.new_v = torch.randn(batch, num_kv_heads, head_dim, generator=dgen, device=device,
+                                 dtype=dtype)
+        pos = lens - 1  # the new token is the last position of each context
+        slots = tables[torch.arange(batch), pos // block_size].long() * block_size + pos % block_size
+        self.slots_host = slots.to(torch.int32)
+        self.tables = tables.to(device)
+        self.lens = lens.to(torch.int32).to(device)
+        self.slots = self.slots_host.to(device)
+        self.out = torch.empty_like(self.query)
+
+    # Algorithmic bytes (what the step must move at minimum).
+    def decode_bytes(self) -> int:
+        es = 2
+        kv = sum(self.lens_list) * self.num_kv_heads * self.head_dim * es * 2
+        qo = 2 * self.batch * self.num_heads * self.head_dim * es
+        table = sum(-(-n // self.block_size) for n in self.lens_list) * 4
+        return kv + qo + table + self.batch * 4
+
+    def append_bytes(self) -> int:
+        return 2 * 2 * self.batch * self.num_kv_heads * self.head_dim * 2 + self.batch * 4
+
+    def step(self):
+        from inferkernellab_b200 import append_kv, paged_decode_attention
+
+        append_kv(self.new_k, self.new_v, self.cache, self.slots)
+        paged_decode_attention(self.query, self.cache, self.tables, self.lens,
+                               validate_inputs=False, out=self.out)
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = ""
+        return False
+
+    def summary(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = [r.split(",") for r in getattr(self, "out", "").strip().splitlines() if r.strip()]
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, r[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "window": "nvidia-smi every 50 ms over warm-up + timed steps"}
+
+
+# ------------------------------------------------------------------ helpers
+
+def _peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def _ncu_traffic() -> float | None:
+    """DRAM bytes per decode launch from the committed ncu summary, if present."""
+    path = ROOT / "profiles" / "decode_config3_ncu.md"
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", path.read_text())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _barrier_sync(world):
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def _max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ arms
+
+def run_ours(args, world, rank, local) -> dict | None:
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    wl = Workload(seed=args.seed + 1000 * rank, device=device)
+    step_bytes = wl.decode_bytes() + wl.append_bytes()
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        wl.step()
+    from inferkernellab_b200 import append_kv, check_device_errors, paged_decode_attention
+
+    if check_device_errors() & ~8:
+        raise RuntimeError("device error word set during warm-up")
+    # ---- device-resident timed region ----
+    k_steps = args.steps
+    dec_start = [torch.cuda.Event(enable_timing=True) for _ in range(k_steps)]
+    dec_end = [torch.cuda.Event(enable_timing=True) for _ in range(k_steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        for _ in range(max(3, args.warmup // 4)):
+            wl.step()
+        _barrier_sync(world)
+        t0.record(stream)
+        for i in range(k_steps):
+            append_kv(wl.new_k, wl.new_v, wl.cache, wl.slots)
+            dec_start[i].record(stream)
+            paged_decode_attention(wl.query, wl.cache, wl.tables, wl.lens, validate_inputs=False,
+                                   out=wl.out)
+            dec_end[i].record(stream)
+        t1.record(stream)
+        _barrier_sync(world)
+    elapsed_ms = _max_over_ranks(t0.elapsed_time(t1), world, device)
+    dec_ms = sum(a.elapsed_time(b) for a, b in zip(dec_start, dec_end)) / k_steps
+    # ---- end-to-end through the public API with host buffers ----
+    pin = dict(pin_memory=True)
+    q_h = wl.query.cpu().pin_memory()
+    k_h, v_h = wl.new_k.cpu().pin_memory(), wl.new_v.cpu().pin_memory()
+    tab_h = wl.tables_host.pin_memory()
+    len_h = torch.tensor(wl.lens_list, dtype=torch.int32).pin_memory()
+    slot_h = wl.slots_host.pin_memory()
+    out_h = torch.empty(wl.query.shape, dtype=wl.dtype, **pin)
+    d_q, d_k, d_v = torch.empty_like(wl.query), torch.empty_like(wl.new_k), torch.empty_like(wl.new_v)
+    d_tab, d_len, d_slot = torch.empty_like(wl.tables), torch.empty_like(wl.lens), torch.empty_like(wl.slots)
+    d_out = torch.empty_like(wl.query)
+    h2d = sum(t.numel() * t.element_size() for t in (q_h, k_h, v_h, tab_h, len_h, slot_h))
+    d2h = out_h.numel() * out_h.element_size()
+
+    def e2e_step():
+        d_q.copy_(q_h, non_blocking=True)
+        d_k.copy_(k_h, non_blocking=True)
+        d_v.copy_(v_h, non_blocking=True)
+        d_tab.copy_(tab_h, non_blocking=True)
+        d_len.copy_(len_h, non_blocking=True)
+        d_slot.copy_(slot_h, non_blocking=True)
+        append_kv(d_k, d_v, wl.cache, d_slot)
+        paged_decode_attention(d_q, wl.cache, d_tab, d_len, validate_inputs=False, out=d_out)
+        out_h.copy_(d_out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    _barrier_sync(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(k_steps):
+        e2e_step()
+    e1.record(stream)
+    _barrier_sync(world)
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1), world, device)
+    errors = check_device_errors()
+    if errors & ~8:
+        raise RuntimeError(f"device error word {errors:#x} after the timed region")
+
+    if rank != 0:
+        return None
+    peak, peak_kind = _peaks()
+    achieved = wl.decode_bytes() / (dec_ms * 1e-3) / 1e9
+    total_bytes = step_bytes * k_steps * world
+    value = total_bytes / (elapsed_ms * 1e-3) / 1e9
+    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
+    record = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": k_steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(elapsed_ms / k_steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V/Q, seeded U[1,8192] context lengths)",
+        "config": {
+            "workload": WORKLOAD,
+            "batch_per_gpu": wl.batch,
+            "sum_ctx_rank0": sum(wl.lens_list),
+            "num_blocks_rank0": wl.cache.layout.num_blocks,
+            "step_bytes_rank0": step_bytes,
+            "l2": "no flush: 1.08 GB working set per step is >8x the 126 MB L2",
+            "parallelism": f"request-partitioned dp{world}, no data-path collective",
+            "seed": args.seed,
+        },
+        "decode_tok_s": round(wl.batch * world * k_steps / (elapsed_ms * 1e-3), 1),
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "paged_decode_kernel<BF16,128,1>",
+            "achieved": round(achieved, 2),
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": round(achieved / peak, 4),
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+            else "fallback 6650 GB/s",
+            "traffic": _ncu_traffic(),
+            "algorithmic_bytes_per_launch": wl.decode_bytes(),
+            "avg_launch_ms": round(dec_ms, 5),
+            "frac_of_nominal_8TBs": round(achieved / 8000.0, 4),
+        },
+        "e2e": {
+            "value": round(e2e_value, 2),
+            "unit": "GB/s",
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "ms_per_step": round(e2e_ms / k_steps, 5),
+            "api": "inferkernellab_b200.append_kv + paged_decode_attention, pinned host buffers",
+        },
+        "gpu_launches": 2 * k_steps,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        record["cpu_baseline"] = cpu_baseline(wl, budget_s=args.cpu_budget)
+    return record
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    """bfloat16 tensor -> numpy uint16 bit patterns (the oracle's bf16 storage)."""
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def workload_lens(seed: int, batch: int = 64, max_ctx: int = 8192) -> list[int]:
+    """The context lengths Workload(seed) draws (same generator, same order)."""
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randint(1, max_ctx + 1, (batch,), generator=gen).tolist()
+
+
+def _oracle_sample_from(wl: Workload, max_tokens: int):
+    """Copy the first requests of a GPU workload (up to max_tokens of context) to host numpy."""
+    chosen, total = [], 0
+    for b, n in enumerate(wl.lens_list):
+        if chosen and total + n > max_tokens:
+            break
+        chosen.append(b)
+        total += n
+    bs = wl.block_size
+    blocks, tables = [], []
+    for b in chosen:
+        need = -(-wl.lens_list[b] // bs)
+        tables.append(list(range(len(blocks), len(blocks) + need)))
+        blocks.extend(wl.tables_host[b, :need].tolist())
+    idx = torch.tensor(blocks, dtype=torch.long, device=wl.cache.k.device)
+    return (_bits(wl.query[chosen]), _bits(wl.cache.k[:, idx]), _bits(wl.cache.v[:, idx]), tables,
+            [wl.lens_list[b] for b in chosen])
+
+
+def _oracle_sample_host(seed: int, max_tokens: int, num_heads=32, num_kv_heads=8, head_dim=128,
+                        block_size=16):
+    """The same requests, generated on the host only (for the CPU reference arm)."""
+    lens_all = workload_lens(seed)
+    lens, total = [], 0
+    for n in lens_all:
+        if lens and total + n > max_tokens:
+            break
+        lens.append(n)
+        total += n
+    need = [-(-n // block_size) for n in lens]
+    rng = np.random.default_rng(seed)
+    nb = sum(need)
+    perm = rng.permutation(nb)
+    tables, cur = [], 0
+    for n in need:
+        tables.append(perm[cur:cur + n].tolist())
+        cur += n
+    shape = (1, nb, block_size, num_kv_heads, head_dim)
+    k = _bits(torch.from_numpy(rng.standard_normal(shape, dtype=np.float32)).bfloat16())
+    v = _bits(torch.from_numpy(rng.standard_normal(shape, dtype=np.float32)).bfloat16())
+    q = _bits(torch.from_numpy(
+        rng.standard_normal((len(lens), num_heads, head_dim), dtype=np.float32)).bfloat16())
+    return q, k, v, tables, lens
+
+
+def _oracle_bytes(lens, num_heads=32, num_kv_heads=8, head_dim=128, block_size=16) -> int:
+    es = 2
+    return (sum(lens) * num_kv_heads * head_dim * es * 2 + 2 * len(lens) * num_heads * head_dim * es
+            + sum(-(-n // block_size) for n in lens) * 4 + len(lens) * 4)
+
+
+def _time_oracle(q, k, v, tables, lens, threads: int) -> float:
+    import oracle  # the CPU restatement: only the baseline legs of this file use it
+
+    def one(b):
+        return oracle.paged_decode_attention(q[b:b + 1], k, v, "bf16", [tables[b]], [lens[b]])
+
+    t = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        list(pool.map(one, range(len(lens))))
+    return time.perf_counter() - t
+
+
+def cpu_baseline(wl: Workload, budget_s: float) -> dict:
+    """The reference algorithm (numpy restatement) on host cores, bounded sample."""
+    threads = os.cpu_count() or 1
+    q, k, v, tables, lens = _oracle_sample_from(wl, max_tokens=4096)
+    probe = _time_oracle(q, k, v, tables, lens, threads)
+    per_token = probe / max(1, sum(lens))
+    target_tokens = int(budget_s / max(per_token, 1e-9))
+    q, k, v, tables, lens = _oracle_sample_from(wl, max_tokens=max(4096, target_tokens))
+    secs = _time_oracle(q, k, v, tables, lens, threads)
+    gbs = _oracle_bytes(lens) / secs / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"first {len(lens)} of the 64 requests of rank 0 ({sum(lens)} context "
+                      f"tokens), numpy float32 restatement of paged_decode_attention, "
+                      f"{threads} threads, {secs:.2f} s"}
+
+
+def run_reference(args, world, rank) -> dict | None:
+    """CPU reference arm: the reference algorithm on host cores, same metric and config."""
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    probe = _oracle_sample_host(args.seed, max_tokens=2048)
+    per_token = _time_oracle(*probe, threads) / max(1, sum(probe[4]))
+    # Size each step so that warm-up + steps end within about two minutes.
+    per_step_s = 120.0 / (args.steps + min(args.warmup, 3))
+    tokens = int(min(8192 * 4, max(64, per_step_s / max(per_token, 1e-9))))
+    q, k, v, tables, lens = _oracle_sample_host(args.seed, max_tokens=tokens)
+    for _ in range(min(args.warmup, 3)):
+        _time_oracle(q, k, v, tables, lens, threads)
+    secs = [_time_oracle(q, k, v, tables, lens, threads) for _ in range(args.steps)]
+    total = sum(secs)
+    gbs = _oracle_bytes(lens) * len(secs) / total / 1e9
+    sample = (f"first {len(lens)} requests of the config-3 batch ({sum(lens)} context tokens) per "
+              f"step, numpy float32 restatement of the reference paged_decode_attention, "
+              f"{threads} threads")
+    return {
+        "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / len(secs) * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference", "config": {"workload": WORKLOAD, "sample": sample},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main(argv=None) -> int:
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=2000)
+    parser.add_argument("--warmup", type=int, default=20)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--seed", type=int, default=0)
+    parser.add_argument("--cpu-budget", type=float, default=10.0,
+                        help="seconds of CPU work for the cpu_baseline sample")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args(argv)
+    if args.warmup < 3:
+        parser.error("--warmup must be >= 3")
+    world, rank, local = _dist()
+    if world != args.gpus and world > 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    if args.impl == "reference":
+        record = run_reference(args, world, rank)
+        if record:
+            print(json.dumps(record), flush=True)
+        return 0
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    try:
+        record = run_ours(args, world, rank, local)
+        if record:
+            print(json.dumps(record), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,208 @@
+/*
+ * b200_paged_attn.h -- C ABI of the B200 (sm_100a) paged-KV attention library.
+ *
+ * Build:  nvcc -gencode arch=compute_100a,code=sm_100a -shared ... -> libb200_paged_attn.so
+ *
+ * Conventions
+ *   - Plain device pointers and sizes only; no framework types cross this ABI.
+ *   - Every entry point returns B200_OK (0) or a negative status code; no
+ *     exception or abort crosses the ABI.  b200_last_error() returns the
+ *     message of the calling thread's last failure.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     All work is enqueued on it; no entry point synchronises the host except
+ *     b200_read_error_word and the b200_validate_* helpers, which say so.
+ *   - The KV cache layout is the reference's PagedKVCache storage
+ *     (reference src/inferkernellab/cache.py:75-94): one contiguous tensor per K
+ *     and V of shape [num_layers, num_blocks, block_size, num_kv_heads, head_dim].
+ *   - Element types: float16 or bfloat16 (B200_F16 / B200_BF16).  Index arrays
+ *     (block tables, lengths, slots) may be int32 or int64 (B200_I32 / B200_I64),
+ *     like the reference wrappers accept (reference triton_ops.py:446-449).
+ */
+#ifndef B200_PAGED_ATTN_H
+#define B200_PAGED_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200_API __attribute__((visibility("default")))
+#else
+#define B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { B200_F16 = 0, B200_BF16 = 1 };
+enum { B200_I32 = 0, B200_I64 = 1 };
+
+enum {
+  B200_OK = 0,
+  B200_ERR_INVALID = -1,     /* bad shape / dtype / metadata  (Python: ValueError)   */
+  B200_ERR_LAYER = -2,       /* layer index out of range       (Python: IndexError)   */
+  B200_ERR_UNSUPPORTED = -3, /* shape this build does not cover (Python: ValueError)  */
+  B200_ERR_WORKSPACE = -4,   /* workspace missing or too small (Python: RuntimeError) */
+  B200_ERR_CUDA = -5,        /* CUDA runtime / driver failure  (Python: RuntimeError) */
+  B200_ERR_DEVICE = -6       /* device error word was set      (Python: RuntimeError) */
+};
+
+/* Device error word bits (see b200_read_error_word). */
+enum {
+  B200_DEVERR_WAIT_FULL = 1,  /* a consumer gave up waiting for a TMA stage (bounded wait) */
+  B200_DEVERR_WAIT_EMPTY = 2, /* a producer gave up waiting for a free stage               */
+  B200_DEVERR_BAD_SLOT = 4,   /* append skipped a slot outside [0, num_blocks*block_size)  */
+  B200_DEVERR_BAD_BLOCK = 8,  /* a block-table entry outside [0, num_blocks) was masked    */
+  B200_DEVERR_DRAIN = 16      /* a producer gave up draining its copies after an abort     */
+};
+
+/* One paged KV cache (both K and V), reference layout, contiguous. */
+typedef struct {
+  void* k_cache;
+  void* v_cache;
+  int32_t num_layers;
+  int32_t num_blocks; /* physical blocks per layer */
+  int32_t block_size; /* tokens per block          */
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t dtype; /* B200_F16 or B200_BF16 */
+} b200_cache_desc;
+
+/* ------------------------------------------------------------------ decode
+ * Paged decode attention: out[b, h, :] = softmax(q[b,h]·K_b^T·scale)·V_b over
+ * the first context_lens[b] logical tokens of request b, K_b/V_b read through
+ * block_tables[b, :] for kv head h / (num_q_heads / num_kv_heads).
+ *
+ * Replaces the reference's paged_decode_attention_triton /
+ * paged_decode_attention_triton_grouped kernels and launch wrappers
+ * (reference src/inferkernellab/triton_ops.py:80-167, 170-401, 404-610); the
+ * math is the reference oracle paged_decode_attention (attention.py:134-175).
+ * Same masking rules as the reference kernels: tokens past table_width *
+ * block_size and tokens whose block id is outside [0, num_blocks) are skipped
+ * (triton_ops.py:129-138).  A request with context_len <= 0 gets NaN output.
+ *
+ * Requirements: head_dim in {16, 32, 64, 128}; num_q_heads a multiple of
+ * num_kv_heads with at most 64 query heads per KV head; block_size a power of
+ * two <= 256 with block_size * head_dim * 2 a multiple of 128 bytes; q/out rows
+ * contiguous in head_dim; num_seqs <= 8192.
+ *
+ * Workspace: `workspace` must hold b200_paged_decode_workspace_bytes() bytes
+ * and be ZERO-FILLED before its first use; the kernel leaves it in that state
+ * again when it completes (split counters reset themselves).  Calls that share
+ * one workspace must be ordered (same stream, or synchronised).
+ */
+typedef struct {
+  int32_t num_seqs;    /* B                                 */
+  int32_t num_q_heads; /* Hq                                */
+  int32_t table_width; /* W: columns of block_tables        */
+  int32_t layer;       /* cache layer to read               */
+  int64_t q_stride_seq, q_stride_head;     /* elements */
+  int64_t out_stride_seq, out_stride_head; /* elements */
+  int64_t table_stride;                    /* elements between block_tables rows */
+  int32_t table_dtype;                     /* B200_I32 / B200_I64 */
+  int32_t lens_dtype;                      /* B200_I32 / B200_I64 */
+  float scale;                             /* softmax scale (reference default head_dim^-0.5) */
+} b200_decode_args;
+
+B200_API size_t b200_paged_decode_workspace_bytes(const b200_cache_desc* cache, const b200_decode_args* args);
+
+B200_API int b200_paged_decode(const b200_cache_desc* cache, const b200_decode_args* args, const void* query,
+                      const void* block_tables, const void* context_lens, void* out,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ append
+ * Reshape-and-cache: cache[layer, slot/BS, slot%BS, h, :] = key[t, h, :] (and V)
+ * for every token t, bit-exact.  Replaces the reference's append_kv_triton and
+ * _append_kv_kernel (reference src/inferkernellab/append.py:19-106) and the
+ * torch scatter PagedKVCache.write_slots (cache.py:156-189).  Negative slots
+ * are skipped (padding); slots >= num_blocks*block_size are skipped and set
+ * B200_DEVERR_BAD_SLOT in *error_word when error_word is not NULL.
+ */
+B200_API int b200_append_kv(const b200_cache_desc* cache, int32_t layer, const void* key, const void* value,
+                   int64_t num_tokens, int64_t key_stride_token, int64_t key_stride_head,
+                   int64_t value_stride_token, int64_t value_stride_head, const void* slots,
+                   int32_t slots_dtype, uint32_t* error_word, void* stream);
+
+/* ----------------------------------------------------------------- prefill
+ * Ragged causal prefill attention over the paged cache.  Sequence b owns the
+ * query tokens of logical positions query_starts[b] .. context_lens[b]-1; a
+ * query at position p attends cache keys 0..p of sequence b (the cache must
+ * already hold them -- append first).  Replaces the reference's
+ * paged_prefill_attention_sdpa (reference src/inferkernellab/attention.py:230-321).
+ *
+ * query_layout 0 (padded, the reference signature): query/out [B, Hq, T, D]
+ *   with T = max_query_len; padded rows t >= context_lens[b]-query_starts[b]
+ *   attend key 0 only, exactly like the reference's mask (attention.py:313).
+ * query_layout 1 (packed): query/out [total_query_tokens, Hq, D]; sequence b
+ *   owns rows cu_seqlens_q[b] .. cu_seqlens_q[b+1]-1 (int32 [B+1]).
+ * error_word (device uint32, may be NULL) collects B200_DEVERR_* bits.
+ */
+typedef struct {
+  int32_t num_seqs;
+  int32_t num_q_heads;
+  int32_t table_width;
+  int32_t layer;
+  int32_t query_layout;       /* 0 = padded, 1 = packed          */
+  int32_t max_query_len;      /* T (padded) / longest range      */
+  int64_t total_query_tokens; /* rows of a packed query          */
+  int64_t q_stride_seq, q_stride_head, q_stride_token; /* elements; stride_seq unused when packed */
+  int64_t o_stride_seq, o_stride_head, o_stride_token;
+  int64_t table_stride;
+  int32_t table_dtype; /* B200_I32 / B200_I64 */
+  int32_t index_dtype; /* dtype of query_starts / context_lens */
+  float scale;
+} b200_prefill_args;
+
+B200_API int b200_paged_prefill(const b200_cache_desc* cache, const b200_prefill_args* args,
+                       const void* query, const void* block_tables, const void* query_starts,
+                       const void* context_lens, const int32_t* cu_seqlens_q, void* out,
+                       uint32_t* error_word, void* stream);
+
+/* --------------------------------------------------------------- metadata
+ * GPU metadata builder for a scheduled batch (token-budget packing moved onto
+ * the device).  For each sequence b the logical range starts[b] .. ends[b]-1 is
+ * mapped through block_tables[b, :] to physical slots
+ *     slot = table[b][p / block_size] * block_size + p % block_size
+ * exactly like PagedKVCache.slot_mapping (reference cache.py:113-129), packed
+ * in sequence order into slots_out (total_tokens entries), and cu_seqlens_out
+ * (int32 [B+1], may be NULL) receives the prefix sums of ends - starts.
+ * A position whose logical block is past table_width or whose block id is
+ * outside [0, num_blocks) gets slot -1 and sets B200_DEVERR_BAD_BLOCK.
+ */
+B200_API int b200_build_slot_mapping(const void* block_tables, int32_t table_dtype, int64_t table_stride,
+                            int32_t table_width, const void* starts, const void* ends,
+                            int32_t index_dtype, int32_t num_seqs, int32_t block_size,
+                            int32_t num_blocks, void* slots_out, int32_t slots_dtype,
+                            int64_t total_tokens, int32_t* cu_seqlens_out, uint32_t* error_word,
+                            void* stream);
+
+/* ------------------------------------------------------------- validation
+ * Device-side form of the reference wrappers' validate_inputs checks
+ * (reference triton_ops.py:450-457).  Writes three int32 flags to flags_out
+ * (device memory): [0] some context_len <= 0, [1] some context_len >
+ * table_width*block_size, [2] some block-table entry outside [0, num_blocks).
+ * Asynchronous; the caller reads flags_out.
+ */
+B200_API int b200_validate_decode_metadata(const void* block_tables, int32_t table_dtype,
+                                  int64_t table_stride, int32_t table_width,
+                                  const void* context_lens, int32_t lens_dtype, int32_t num_seqs,
+                                  int32_t block_size, int32_t num_blocks, int32_t* flags_out,
+                                  void* stream);
+
+/* --------------------------------------------------------------- utilities */
+
+/* Synchronises `stream`, reads the uint32 device error word at `error_word`
+ * into *value, and (if clear != 0) zeroes it.  Host-blocking. */
+B200_API int b200_read_error_word(uint32_t* error_word, uint32_t* value, int32_t clear, void* stream);
+
+/* Message of this thread's last failure ("" if none). */
+B200_API const char* b200_last_error(void);
+
+/* Library version string. */
+B200_API const char* b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_PAGED_ATTN_H */

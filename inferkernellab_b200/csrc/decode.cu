@@ -1,0 +1,624 @@
+// Paged decode attention for sm_100a: split-KV over a persistent stream-K grid.
+//
+// Work decomposition
+//   A *segment* is one (request r, kv head h) pair; it owns ceil(len_r / 64)
+//   *tiles* of 64 logical tokens.  All segments are laid end to end (request
+//   major, then kv head) and the resulting tile range is cut into gridDim.x
+//   equal contiguous pieces, one per CTA ("stream-K").  A CTA therefore walks
+//   whole segments plus at most one partial segment at each end, and every CTA
+//   moves the same number of K/V bytes whatever the context-length spread.
+//   A segment covered by one CTA is written straight to `out`; a segment split
+//   over several CTAs writes a partial (normalised O and log-sum-exp) into the
+//   workspace, and the CTA that arrives last on the segment's counter merges the
+//   partials and resets the counter -- no second kernel, no spin waiting.
+//
+// Inside a CTA
+//   warp 4 (producer): reads the block table for each tile and issues TMA tile
+//     loads of the K and V page rows of head h into a STAGES-deep shared-memory
+//     ring (mbarrier full/empty pipeline, bounded waits);
+//   warps 0..3 (consumers): the G = Hq/Hkv query heads of the segment form the
+//     M dimension of mma.sync m16n8k16 tiles (padded to 16 rows per m-tile);
+//     S = Q K^T and O += P V run on the tensor cores with fp32 accumulation and
+//     a base-2 online softmax.  Each consumer warp owns a token slice of every
+//     tile; the slices are merged through shared memory at segment end.
+//
+// Masking (reference triton_ops.py:128-165): tokens at or past the context
+// length, and tokens of pages whose block id is outside [0, num_blocks), get
+// score -inf and their V rows are zeroed in registers, so NaN/Inf left in
+// unwritten cache slots never reaches the output.
+#include <math.h>
+
+#include "../../include/b200_paged_attn.h"
+#include "attn_core.cuh"
+#include "common.cuh"
+#include "decode.h"
+#include "host_common.h"
+
+namespace b200 {
+
+constexpr int kDecTile = kKvTile;
+constexpr int kDecConsumerWarps = 4;
+constexpr int kDecThreads = (kDecConsumerWarps + 1) * 32;
+constexpr int kDecMaxSeqs = 8192;
+
+struct DecodeParams {
+  const void* q;
+  void* out;
+  const void* tables;
+  const void* lens;
+  uint32_t* err;
+  int* counters;
+  float* part_lse;
+  float* part_o;
+  long long q_stride_seq, q_stride_head;
+  long long out_stride_seq, out_stride_head;
+  long long table_stride;
+  long long layer_slot_base;
+  int num_seqs, num_kv_heads, group, table_width;
+  int num_blocks, block_size;
+  int box_rows, sw_mask;
+  int table64, lens64;
+  float scale_log2;
+};
+
+template <int D>
+struct DecodeShape : KvTileShape<D> {
+  static constexpr int kStages = D >= 128 ? 3 : 4;
+};
+
+// Shared-memory carve-up (offsets from a 1024-byte aligned base).
+struct DecodeSmem {
+  int stage_bytes;     // K + V of one stage
+  int bars_off;        // full[S], empty[S]
+  int mask_off;        // uint64 per stage
+  int flags_off;       // abort, merge flag
+  int red_m_off, red_l_off, red_o_off;
+  int len_off, begin_off, scan_off;
+  int total;
+};
+
+template <int D, int MT>
+__host__ __device__ inline DecodeSmem decode_smem_layout(int group, int num_seqs) {
+  using S = DecodeShape<D>;
+  constexpr int kSlices = kDecConsumerWarps / MT;
+  DecodeSmem L;
+  L.stage_bytes = 2 * S::kTileBytes;
+  int off = S::kStages * L.stage_bytes;
+  L.bars_off = off;
+  off += 2 * S::kStages * 8;
+  L.mask_off = off;
+  off += S::kStages * 8;
+  L.flags_off = off;
+  off += 16;
+  L.red_m_off = off;
+  off += kSlices * 16 * MT * 4;
+  L.red_l_off = off;
+  off += kSlices * 16 * MT * 4;
+  off = (off + 15) & ~15;
+  L.red_o_off = off;
+  off += kSlices * group * D * 4;
+  L.len_off = off;
+  off += num_seqs * 4;
+  L.begin_off = off;
+  off += (num_seqs + 1) * 4;
+  L.scan_off = off;
+  off += kDecThreads * 4;
+  L.total = off;
+  return L;
+}
+
+// Walks tiles in global order: request-major, then kv head, then tile.
+struct TileCursor {
+  int r, h, t, nt;
+  __device__ void init(int tile, const int* begin, const int* lens, int num_seqs, int hkv) {
+    int lo = 0, hi = num_seqs;
+    while (hi - lo > 1) {
+      int mid = (lo + hi) >> 1;
+      if (begin[mid] <= tile) lo = mid; else hi = mid;
+    }
+    r = lo;
+    nt = (lens[r] + kDecTile - 1) / kDecTile;
+    int local = tile - begin[r];
+    h = local / nt;
+    t = local - h * nt;
+    (void)hkv;
+  }
+  __device__ void advance(const int* lens, int num_seqs, int hkv) {
+    if (++t < nt) return;
+    t = 0;
+    if (++h < hkv) return;
+    h = 0;
+    do {
+      ++r;
+    } while (r < num_seqs && lens[r] == 0);
+    nt = r < num_seqs ? (lens[r] + kDecTile - 1) / kDecTile : 0;
+  }
+};
+
+__device__ __forceinline__ float fast_log2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename E, int D, int MT>
+__global__ void __launch_bounds__(kDecThreads, 2)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
+  using S = DecodeShape<D>;
+  using T = typename E::T;
+  constexpr int kSlices = kDecConsumerWarps / MT;
+  constexpr int kTokPerWarp = kDecTile / kSlices;  // 16, 32 or 64
+  constexpr int kGroups16 = kTokPerWarp / 16;
+  constexpr int kStages = S::kStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const DecodeSmem L = decode_smem_layout<D, MT>(p.group, p.num_seqs);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bars_off);
+  uint64_t* empty_bar = full_bar + kStages;
+  uint64_t* stage_mask = reinterpret_cast<uint64_t*>(smem + L.mask_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.flags_off);
+  int* merge_flag = reinterpret_cast<int*>(smem + L.flags_off + 4);
+  float* red_m = reinterpret_cast<float*>(smem + L.red_m_off);
+  float* red_l = reinterpret_cast<float*>(smem + L.red_l_off);
+  float* red_o = reinterpret_cast<float*>(smem + L.red_o_off);
+  int* len_s = reinterpret_cast<int*>(smem + L.len_off);
+  int* begin_s = reinterpret_cast<int*>(smem + L.begin_off);
+  int* scan_s = reinterpret_cast<int*>(smem + L.scan_off);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int B = p.num_seqs;
+  const int HKV = p.num_kv_heads;
+  const int G = p.group;
+
+  // ---- prologue: effective lengths and the tile prefix over requests ----
+  const long long cap = static_cast<long long>(p.table_width) * p.block_size;
+  for (int i = tid; i < B; i += kDecThreads) {
+    long long len = load_index(p.lens, i, p.lens64);
+    len = len < 0 ? 0 : (len > cap ? cap : len);
+    len_s[i] = static_cast<int>(len);
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kDecConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kDecConsumerWarps && lane == 0) {
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+  __syncthreads();
+  {
+    const int chunk = (B + kDecThreads - 1) / kDecThreads;
+    const int lo = tid * chunk;
+    const int hi = min(B, lo + chunk);
+    int sum = 0;
+    for (int i = lo; i < hi; ++i) sum += ((len_s[i] + kDecTile - 1) / kDecTile) * HKV;
+    scan_s[tid] = sum;
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      for (int i = 0; i < kDecThreads; ++i) {
+        int v = scan_s[i];
+        scan_s[i] = acc;
+        acc += v;
+      }
+      begin_s[B] = acc;
+    }
+    __syncthreads();
+    int acc = scan_s[tid];
+    for (int i = lo; i < hi; ++i) {
+      begin_s[i] = acc;
+      acc += ((len_s[i] + kDecTile - 1) / kDecTile) * HKV;
+    }
+  }
+  __syncthreads();
+
+  // Requests with no readable token: NaN, like 0/0 in the reference kernel.
+  if (blockIdx.x == 0 && warp < kDecConsumerWarps) {
+    for (int r = 0; r < B; ++r) {
+      if (len_s[r] != 0) continue;
+      const int nh = HKV * G;
+      for (int i = tid; i < nh * D; i += kDecConsumerWarps * 32) {
+        const int hq = i / D, d = i - hq * D;
+        reinterpret_cast<T*>(p.out)[r * p.out_stride_seq + hq * p.out_stride_head + d] =
+            from_float<E>(__int_as_float(0x7fc00000));
+      }
+    }
+  }
+
+  const int total = begin_s[B];
+  const int per_cta = (total + gridDim.x - 1) / gridDim.x;
+  const int my_begin = min(total, static_cast<int>(blockIdx.x) * per_cta);
+  const int my_end = min(total, my_begin + per_cta);
+  const int n_tiles = my_end - my_begin;
+  if (n_tiles <= 0) return;
+
+  const uint32_t smem_base = smem_u32(smem);
+
+  if (warp == kDecConsumerWarps) {
+    // =============================== producer ===============================
+    PagedSource src;
+    src.tables = p.tables;
+    src.table_stride = p.table_stride;
+    src.layer_slot_base = p.layer_slot_base;
+    src.table64 = p.table64;
+    src.num_blocks = p.num_blocks;
+    src.block_size = p.block_size;
+    src.box_rows = p.box_rows;
+    TileCursor cur;
+    cur.init(my_begin, begin_s, len_s, B, HKV);
+    int issued = 0;
+    for (int it = 0; it < n_tiles; ++it) {
+      const int s = it % kStages;
+      const uint32_t k = static_cast<uint32_t>(it / kStages);
+      if (!mbar_wait_bounded(&empty_bar[s], (k & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty))
+        break;
+      const int tok0 = cur.t * kDecTile;
+      const int ntok = min(kDecTile, len_s[cur.r] - tok0);
+      uint8_t* kdst = smem + s * L.stage_bytes;
+      issue_kv_tile<D>(&kmap, &vmap, src, cur.r, cur.h, tok0, ntok, kdst, kdst + S::kTileBytes,
+                       &full_bar[s], &stage_mask[s], p.err, lane);
+      ++issued;
+      cur.advance(len_s, B, HKV);
+    }
+    // Drain: the last phases this warp armed must complete before the CTA
+    // exits (bounded; only waits after an abort left stages unconsumed).
+    if (lane == 0) drain_stages<kStages>(full_bar, issued, p.err);
+    return;
+  }
+
+  // ================================ consumers ================================
+  const int mt = warp % MT;
+  const int slice = warp / MT;
+  const int g = lane >> 2;
+  const int tq = lane & 3;
+  const int row0 = mt * 16 + g;  // query-head row inside the group
+  const int row1 = row0 + 8;
+  const uint32_t sw = static_cast<uint32_t>(p.sw_mask);
+
+  uint32_t qf[D / 16][4];
+  float o[D / 8][4];
+  float m_r[2], l_r[2];
+  bool aborted = false;
+
+  TileCursor cur;
+  cur.init(my_begin, begin_s, len_s, B, HKV);
+  bool seg_start = true;
+
+  for (int it = 0; it < n_tiles; ++it) {
+    if (seg_start) {
+      seg_start = false;
+      const T* qb = reinterpret_cast<const T*>(p.q) + cur.r * p.q_stride_seq +
+                    static_cast<long long>(cur.h * G) * p.q_stride_head;
+      load_q_frag<E, D>(qf, row0 < G ? qb + row0 * p.q_stride_head : nullptr,
+                        row1 < G ? qb + row1 * p.q_stride_head : nullptr, tq);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      m_r[0] = m_r[1] = -INFINITY;
+      l_r[0] = l_r[1] = 0.f;
+    }
+
+    const int s = it % kStages;
+    const uint32_t k = static_cast<uint32_t>(it / kStages);
+    if (!aborted && !mbar_wait_bounded(&full_bar[s], k & 1u, abort_flag, p.err, kErrWaitFull))
+      aborted = true;
+
+    if (!aborted) {
+      const uint64_t tmask = stage_mask[s];
+      const uint32_t kbase = smem_base + s * L.stage_bytes;
+      const uint32_t vbase = kbase + S::kTileBytes;
+#pragma unroll
+      for (int gi = 0; gi < kGroups16; ++gi) {
+        const int tok = slice * kTokPerWarp + gi * 16;  // first tile row of this 16-token group
+        const uint32_t gmask = static_cast<uint32_t>(tmask >> tok) & 0xffffu;
+        if (gmask == 0) continue;
+        attend16<E, D, false>(qf, o, m_r, l_r, kbase, vbase, tok, gmask, 0, 0, 0, p.scale_log2,
+                              sw, lane);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);
+    }
+
+    // ---- segment end: merge the token slices, then finish or publish ----
+    const bool seg_end = (cur.t == cur.nt - 1) || (it == n_tiles - 1);
+    if (seg_end) {
+      const int seg = cur.r * HKV + cur.h;
+      const int seg_begin = begin_s[cur.r] + cur.h * cur.nt;
+      const int seg_end_tile = seg_begin + cur.nt;
+      const bool complete = seg_begin >= my_begin && seg_end_tile <= my_end;
+      const float l0 = quad_sum(l_r[0]);
+      const float l1 = quad_sum(l_r[1]);
+      if (!aborted) {
+        if (tq == 0) {
+          red_m[slice * 16 * MT + row0] = m_r[0];
+          red_m[slice * 16 * MT + row1] = m_r[1];
+          red_l[slice * 16 * MT + row0] = l0;
+          red_l[slice * 16 * MT + row1] = l1;
+        }
+        if (row0 < G) {
+          float* dst = red_o + (slice * G + row0) * D + 2 * tq;
+#pragma unroll
+          for (int i = 0; i < D / 8; ++i)
+            *reinterpret_cast<float2*>(dst + i * 8) = make_float2(o[i][0], o[i][1]);
+        }
+        if (row1 < G) {
+          float* dst = red_o + (slice * G + row1) * D + 2 * tq;
+#pragma unroll
+          for (int i = 0; i < D / 8; ++i)
+            *reinterpret_cast<float2*>(dst + i * 8) = make_float2(o[i][2], o[i][3]);
+        }
+      }
+      named_bar_sync(1, kDecConsumerWarps * 32);
+      const int slot = seg_begin <= my_begin ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
+      if (!aborted) {
+        for (int idx = tid; idx < G * D; idx += kDecConsumerWarps * 32) {
+          const int row = idx / D;
+          const int d = idx - row * D;
+          const int mrow = (row >> 4) * 16 + (row & 15);  // row inside its m-tile block
+          float mmax = -INFINITY;
+#pragma unroll
+          for (int sl = 0; sl < kSlices; ++sl) mmax = fmaxf(mmax, red_m[sl * 16 * MT + mrow]);
+          const float base = mmax == -INFINITY ? 0.f : mmax;
+          float lsum = 0.f, osum = 0.f;
+#pragma unroll
+          for (int sl = 0; sl < kSlices; ++sl) {
+            const float w = fast_exp2(red_m[sl * 16 * MT + mrow] - base);
+            lsum += red_l[sl * 16 * MT + mrow] * w;
+            osum += red_o[(sl * G + row) * D + d] * w;
+          }
+          if (complete) {
+            reinterpret_cast<T*>(p.out)[cur.r * p.out_stride_seq +
+                                        (cur.h * G + row) * p.out_stride_head + d] =
+                from_float<E>(osum / lsum);
+          } else {
+            p.part_o[(static_cast<long long>(slot) * G + row) * D + d] = osum / lsum;
+            if (d == 0) p.part_lse[slot * G + row] = lsum > 0.f ? base + fast_log2(lsum) : -INFINITY;
+          }
+        }
+      }
+      if (!complete) {
+        __threadfence();
+        named_bar_sync(1, kDecConsumerWarps * 32);
+        if (tid == 0) {
+          int last = 0;
+          if (!aborted) {
+            const int p_first = seg_begin / per_cta;
+            const int p_last = (seg_end_tile - 1) / per_cta;
+            const int prev = atomicAdd(&p.counters[seg], 1);
+            last = prev == p_last - p_first;
+          }
+          *merge_flag = last;
+        }
+        named_bar_sync(1, kDecConsumerWarps * 32);
+        if (*merge_flag) {
+          __threadfence();
+          const int p_first = seg_begin / per_cta;
+          const int p_last = (seg_end_tile - 1) / per_cta;
+          for (int idx = tid; idx < G * D; idx += kDecConsumerWarps * 32) {
+            const int row = idx / D;
+            const int d = idx - row * D;
+            float mmax = -INFINITY;
+            for (int q = p_first; q <= p_last; ++q) {
+              const int sl = seg_begin <= q * per_cta ? 2 * q : 2 * q + 1;
+              mmax = fmaxf(mmax, __ldcg(p.part_lse + sl * G + row));
+            }
+            const float base = mmax == -INFINITY ? 0.f : mmax;
+            float wsum = 0.f, osum = 0.f;
+            for (int q = p_first; q <= p_last; ++q) {
+              const int sl = seg_begin <= q * per_cta ? 2 * q : 2 * q + 1;
+              const float lse = __ldcg(p.part_lse + sl * G + row);
+              if (lse == -INFINITY) continue;  // piece saw only masked tokens
+              const float w = fast_exp2(lse - base);
+              wsum += w;
+              osum += w * __ldcg(p.part_o + (static_cast<long long>(sl) * G + row) * D + d);
+            }
+            reinterpret_cast<T*>(p.out)[cur.r * p.out_stride_seq +
+                                        (cur.h * G + row) * p.out_stride_head + d] =
+                from_float<E>(osum / wsum);
+          }
+          if (tid == 0) p.counters[seg] = 0;
+        }
+      }
+      named_bar_sync(1, kDecConsumerWarps * 32);
+      seg_start = true;
+    }
+    cur.advance(len_s, B, HKV);
+  }
+}
+
+// ------------------------------------------------------------------- host
+
+struct WorkspaceLayout {
+  size_t err_off, counters_off, lse_off, o_off, total;
+};
+
+static WorkspaceLayout workspace_layout(int num_seqs, int hkv, int group, int head_dim, int grid) {
+  WorkspaceLayout w;
+  size_t off = 0;
+  w.err_off = off;
+  off += 256;
+  w.counters_off = off;
+  off += ((static_cast<size_t>(num_seqs) * hkv * 4 + 255) / 256) * 256;
+  w.lse_off = off;
+  off += ((static_cast<size_t>(2) * grid * group * 4 + 255) / 256) * 256;
+  w.o_off = off;
+  off += static_cast<size_t>(2) * grid * group * head_dim * 4;
+  w.total = off;
+  return w;
+}
+
+template <typename E, int D, int MT>
+static int launch_decode_t(const CUtensorMap& kmap, const CUtensorMap& vmap,
+                           const DecodeParams& p, int num_sms, int* grid_out, bool dry_run,
+                           cudaStream_t stream) {
+  const DecodeSmem L = decode_smem_layout<D, MT>(p.group, p.num_seqs);
+  const int smem = L.total + 1024;
+  auto kern = paged_decode_kernel<E, D, MT>;
+  static int configured_smem[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && configured_smem[dev] < smem) {
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess) return cuda_status(err, "cudaFuncSetAttribute(decode smem)");
+    configured_smem[dev] = smem;
+  }
+  int per_sm = 0;
+  cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, smem);
+  if (err != cudaSuccess) return cuda_status(err, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  if (per_sm < 1)
+    return set_error(B200_ERR_UNSUPPORTED, "decode kernel does not fit on an SM (shared memory)");
+  const int grid = num_sms * per_sm;
+  *grid_out = grid;
+  if (dry_run) return B200_OK;
+  kern<<<grid, kDecThreads, smem, stream>>>(kmap, vmap, p);
+  return cuda_status(cudaGetLastError(), "paged_decode_kernel launch");
+}
+
+template <typename E, int D>
+static int dispatch_mt(int mt, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                       const DecodeParams& p, int num_sms, int* grid, bool dry, cudaStream_t s) {
+  switch (mt) {
+    case 1: return launch_decode_t<E, D, 1>(kmap, vmap, p, num_sms, grid, dry, s);
+    case 2: return launch_decode_t<E, D, 2>(kmap, vmap, p, num_sms, grid, dry, s);
+    default: return launch_decode_t<E, D, 4>(kmap, vmap, p, num_sms, grid, dry, s);
+  }
+}
+
+template <typename E>
+static int dispatch_d(int d, int mt, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                      const DecodeParams& p, int num_sms, int* grid, bool dry, cudaStream_t s) {
+  switch (d) {
+    case 16: return dispatch_mt<E, 16>(mt, kmap, vmap, p, num_sms, grid, dry, s);
+    case 32: return dispatch_mt<E, 32>(mt, kmap, vmap, p, num_sms, grid, dry, s);
+    case 64: return dispatch_mt<E, 64>(mt, kmap, vmap, p, num_sms, grid, dry, s);
+    default: return dispatch_mt<E, 128>(mt, kmap, vmap, p, num_sms, grid, dry, s);
+  }
+}
+
+static int check_decode_args(const b200_cache_desc* c, const b200_decode_args* a) {
+  if (c == nullptr || a == nullptr) return set_error(B200_ERR_INVALID, "null descriptor");
+  if (c->num_layers <= 0 || c->num_blocks <= 0 || c->block_size <= 0 || c->num_kv_heads <= 0 ||
+      c->head_dim <= 0)
+    return set_error(B200_ERR_INVALID, "cache dimensions must be positive");
+  if (c->dtype != B200_F16 && c->dtype != B200_BF16)
+    return set_error(B200_ERR_UNSUPPORTED, "cache dtype must be float16 or bfloat16");
+  if (c->head_dim != 16 && c->head_dim != 32 && c->head_dim != 64 && c->head_dim != 128)
+    return set_error(B200_ERR_UNSUPPORTED, "head_dim must be one of 16, 32, 64, 128");
+  if ((c->block_size & (c->block_size - 1)) != 0 || c->block_size > 256)
+    return set_error(B200_ERR_UNSUPPORTED, "block_size must be a power of two <= 256");
+  if (a->layer < 0 || a->layer >= c->num_layers)
+    return set_error(B200_ERR_LAYER, "layer is out of range");
+  if (a->num_seqs <= 0 || a->num_q_heads <= 0)
+    return set_error(B200_ERR_INVALID, "query dimensions must be positive");
+  if (a->num_seqs > kDecMaxSeqs)
+    return set_error(B200_ERR_UNSUPPORTED, "decode batch is limited to 8192 sequences");
+  if (a->num_q_heads % c->num_kv_heads != 0)
+    return set_error(B200_ERR_INVALID, "num_heads must be divisible by num_kv_heads");
+  if (a->num_q_heads / c->num_kv_heads > 64)
+    return set_error(B200_ERR_UNSUPPORTED, "at most 64 query heads per kv head");
+  if (a->table_width <= 0)
+    return set_error(B200_ERR_INVALID, "block_tables must contain at least one logical block");
+  const int64_t slots = static_cast<int64_t>(c->num_layers) * c->num_blocks * c->block_size;
+  if (slots >= (1ll << 31)) return set_error(B200_ERR_UNSUPPORTED, "cache has more than 2^31 slots");
+  if (static_cast<int64_t>(a->table_width) * c->block_size >= (1ll << 30))
+    return set_error(B200_ERR_UNSUPPORTED, "block table capacity too large");
+  if ((a->q_stride_seq | a->q_stride_head | a->out_stride_seq | a->out_stride_head) & 1)
+    return set_error(B200_ERR_INVALID, "query/out strides must be even");
+  return B200_OK;
+}
+
+size_t decode_workspace_bytes(const b200_cache_desc* c, const b200_decode_args* a) {
+  clear_error();
+  if (check_decode_args(c, a) != B200_OK) return 0;
+  DeviceInfo info;
+  if (current_device_info(&info) != B200_OK) return 0;
+  const int group = a->num_q_heads / c->num_kv_heads;
+  const int mt = group <= 16 ? 1 : (group <= 32 ? 2 : 4);
+  CUtensorMap dummy;
+  DecodeParams p{};
+  p.group = group;
+  p.num_seqs = a->num_seqs;
+  int grid = 0;
+  int rc = c->dtype == B200_BF16
+               ? dispatch_d<BF16>(c->head_dim, mt, dummy, dummy, p, info.num_sms, &grid, true, 0)
+               : dispatch_d<Half>(c->head_dim, mt, dummy, dummy, p, info.num_sms, &grid, true, 0);
+  if (rc != B200_OK) return 0;
+  return workspace_layout(a->num_seqs, c->num_kv_heads, group, c->head_dim, grid).total;
+}
+
+int launch_paged_decode(const b200_cache_desc* c, const b200_decode_args* a, const void* query,
+                        const void* block_tables, const void* context_lens, void* out,
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  int rc = check_decode_args(c, a);
+  if (rc != B200_OK) return rc;
+  if (!query || !block_tables || !context_lens || !out || !c->k_cache || !c->v_cache)
+    return set_error(B200_ERR_INVALID, "null tensor pointer");
+  if ((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(out)) & 3)
+    return set_error(B200_ERR_INVALID, "query/out must be 4-byte aligned");
+  DeviceInfo info;
+  rc = current_device_info(&info);
+  if (rc != B200_OK) return rc;
+  CacheTmaGeometry geo;
+  std::string why;
+  if (!cache_tma_geometry(c, kDecTile, &geo, &why)) return set_error(B200_ERR_UNSUPPORTED, why);
+  CUtensorMap kmap, vmap;
+  rc = encode_cache_tensor_map(c, c->k_cache, geo, &kmap);
+  if (rc != B200_OK) return rc;
+  rc = encode_cache_tensor_map(c, c->v_cache, geo, &vmap);
+  if (rc != B200_OK) return rc;
+
+  const int group = a->num_q_heads / c->num_kv_heads;
+  const int mt = group <= 16 ? 1 : (group <= 32 ? 2 : 4);
+  DecodeParams p{};
+  p.q = query;
+  p.out = out;
+  p.tables = block_tables;
+  p.lens = context_lens;
+  p.q_stride_seq = a->q_stride_seq;
+  p.q_stride_head = a->q_stride_head;
+  p.out_stride_seq = a->out_stride_seq;
+  p.out_stride_head = a->out_stride_head;
+  p.table_stride = a->table_stride;
+  p.layer_slot_base = static_cast<long long>(a->layer) * c->num_blocks * c->block_size;
+  p.num_seqs = a->num_seqs;
+  p.num_kv_heads = c->num_kv_heads;
+  p.group = group;
+  p.table_width = a->table_width;
+  p.num_blocks = c->num_blocks;
+  p.block_size = c->block_size;
+  p.box_rows = geo.box_rows;
+  p.sw_mask = geo.swizzle_bytes == 0 ? 0 : geo.swizzle_bytes / 16 - 1;
+  p.table64 = a->table_dtype == B200_I64;
+  p.lens64 = a->lens_dtype == B200_I64;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+
+  int grid = 0;
+  rc = c->dtype == B200_BF16
+           ? dispatch_d<BF16>(c->head_dim, mt, kmap, vmap, p, info.num_sms, &grid, true, stream)
+           : dispatch_d<Half>(c->head_dim, mt, kmap, vmap, p, info.num_sms, &grid, true, stream);
+  if (rc != B200_OK) return rc;
+  const WorkspaceLayout w = workspace_layout(a->num_seqs, c->num_kv_heads, group, c->head_dim, grid);
+  if (workspace == nullptr || workspace_bytes < w.total)
+    return set_error(B200_ERR_WORKSPACE, "decode workspace missing or smaller than "
+                                         "b200_paged_decode_workspace_bytes()");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return set_error(B200_ERR_WORKSPACE, "decode workspace must be 256-byte aligned");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.err = reinterpret_cast<uint32_t*>(ws + w.err_off);
+  p.counters = reinterpret_cast<int*>(ws + w.counters_off);
+  p.part_lse = reinterpret_cast<float*>(ws + w.lse_off);
+  p.part_o = reinterpret_cast<float*>(ws + w.o_off);
+  return c->dtype == B200_BF16
+             ? dispatch_d<BF16>(c->head_dim, mt, kmap, vmap, p, info.num_sms, &grid, false, stream)
+             : dispatch_d<Half>(c->head_dim, mt, kmap, vmap, p, info.num_sms, &grid, false, stream);
+}
+
+}  // namespace b200

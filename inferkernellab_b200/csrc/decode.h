@@ -1,0 +1,17 @@
+// Launchers of the paged decode kernel (decode.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+#include "../../include/b200_paged_attn.h"
+
+namespace b200 {
+
+size_t decode_workspace_bytes(const b200_cache_desc* c, const b200_decode_args* a);
+
+int launch_paged_decode(const b200_cache_desc* c, const b200_decode_args* a, const void* query,
+                        const void* block_tables, const void* context_lens, void* out,
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+}  // namespace b200

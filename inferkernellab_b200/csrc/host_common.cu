@@ -1,0 +1,147 @@
+// Host helpers: error strings, per-device properties, TMA tensor maps.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "host_common.h"
+
+namespace b200 {
+
+namespace {
+thread_local std::string g_last_error;
+
+std::mutex g_mu;
+std::vector<DeviceInfo> g_devices;
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+struct MapKey {
+  const void* base;
+  int64_t slots;
+  int heads, dim, dtype, chunk, rows, swz;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && slots == o.slots && heads == o.heads && dim == o.dim &&
+           dtype == o.dtype && chunk == o.chunk && rows == o.rows && swz == o.swz;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = std::hash<const void*>()(k.base);
+    h ^= std::hash<int64_t>()(k.slots) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+    h ^= static_cast<size_t>(k.heads * 131 + k.dim * 7 + k.dtype + k.chunk * 31 + k.rows * 17 +
+                             k.swz * 3);
+    return h;
+  }
+};
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+}  // namespace
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+const char* last_error_cstr() { return g_last_error.c_str(); }
+
+int cuda_status(cudaError_t err, const char* what) {
+  if (err == cudaSuccess) return B200_OK;
+  return set_error(B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+int current_device_info(DeviceInfo* out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_status(err, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (dev >= static_cast<int>(g_devices.size())) g_devices.resize(dev + 1);
+  DeviceInfo& info = g_devices[dev];
+  if (info.device < 0) {
+    int sms = 0, smem = 0;
+    err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (err != cudaSuccess) return cuda_status(err, "cudaDeviceGetAttribute(SM count)");
+    err = cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (err != cudaSuccess) return cuda_status(err, "cudaDeviceGetAttribute(smem)");
+    info.device = dev;
+    info.num_sms = sms;
+    info.max_smem_optin = smem;
+  }
+  *out = info;
+  return B200_OK;
+}
+
+bool cache_tma_geometry(const b200_cache_desc* c, int tile_tokens, CacheTmaGeometry* geo,
+                        std::string* why) {
+  const int row_bytes = c->head_dim * 2;
+  geo->chunk_bytes = row_bytes < 128 ? row_bytes : 128;
+  geo->chunk_elems = geo->chunk_bytes / 2;
+  geo->num_chunks = row_bytes / geo->chunk_bytes;
+  geo->box_rows = c->block_size < tile_tokens ? c->block_size : tile_tokens;
+  const int box_bytes = geo->box_rows * geo->chunk_bytes;
+  if (box_bytes % 128 != 0) {
+    *why = "block_size * head_dim * element_size must be a multiple of 128 bytes "
+           "(TMA destination alignment)";
+    return false;
+  }
+  // Swizzle only when every box starts on a swizzle-atom (1024-byte) boundary
+  // so the pattern seen by the reader is the same however TMA anchors it.
+  geo->swizzle_bytes = (box_bytes % 1024 == 0) ? geo->chunk_bytes : 0;
+  return true;
+}
+
+int encode_cache_tensor_map(const b200_cache_desc* c, const void* base,
+                            const CacheTmaGeometry& geo, CUtensorMap* out) {
+  const int64_t slots =
+      static_cast<int64_t>(c->num_layers) * c->num_blocks * static_cast<int64_t>(c->block_size);
+  MapKey key{base, slots, c->num_kv_heads, c->head_dim, c->dtype, geo.chunk_elems,
+             geo.box_rows, geo.swizzle_bytes};
+  std::lock_guard<std::mutex> lock(g_mu);
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *out = it->second;
+    return B200_OK;
+  }
+  if (g_encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (err != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return set_error(B200_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return set_error(B200_ERR_INVALID, "cache tensor base must be 16-byte aligned");
+  cuuint64_t gdim[3] = {static_cast<cuuint64_t>(c->head_dim),
+                        static_cast<cuuint64_t>(c->num_kv_heads), static_cast<cuuint64_t>(slots)};
+  cuuint64_t gstride[2] = {static_cast<cuuint64_t>(c->head_dim) * 2,
+                           static_cast<cuuint64_t>(c->num_kv_heads) * c->head_dim * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(geo.chunk_elems), 1u,
+                       static_cast<cuuint32_t>(geo.box_rows)};
+  cuuint32_t estride[3] = {1u, 1u, 1u};
+  CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (geo.swizzle_bytes == 32) swz = CU_TENSOR_MAP_SWIZZLE_32B;
+  if (geo.swizzle_bytes == 64) swz = CU_TENSOR_MAP_SWIZZLE_64B;
+  if (geo.swizzle_bytes == 128) swz = CU_TENSOR_MAP_SWIZZLE_128B;
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  CUresult r = g_encode(&map,
+                        c->dtype == B200_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        3, const_cast<void*>(base), gdim, gstride, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(B200_ERR_CUDA,
+                     "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) +
+                         ")");
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps.emplace(key, map);
+  *out = map;
+  return B200_OK;
+}
+
+}  // namespace b200

@@ -1,0 +1,52 @@
+// Host-side helpers shared by the launchers: error reporting, device
+// properties, TMA tensor-map encoding.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/b200_paged_attn.h"
+
+namespace b200 {
+
+// Records `msg` as this thread's last error and returns `code`.
+int set_error(int code, const std::string& msg);
+void clear_error();
+
+// cudaError_t -> B200_ERR_CUDA with a message naming `what`.
+int cuda_status(cudaError_t err, const char* what);
+
+struct DeviceInfo {
+  int device = -1;
+  int num_sms = 0;
+  int max_smem_optin = 0;
+};
+// Properties of the current device (cached per device).
+int current_device_info(DeviceInfo* out);
+
+// Geometry of the 3-D TMA view of one cache tensor:
+//   dim0 = head_dim (contiguous), dim1 = kv heads, dim2 = every token slot of
+//   every layer (num_layers * num_blocks * block_size).
+struct CacheTmaGeometry {
+  int chunk_elems;  // elements of head_dim per TMA box row (<= 128 bytes)
+  int chunk_bytes;
+  int num_chunks;   // head_dim / chunk_elems
+  int box_rows;     // tokens per box
+  int swizzle_bytes;  // 0, 32, 64 or 128
+};
+
+// Chooses the box geometry for a cache and a token tile; returns false with a
+// message if the layout cannot be expressed (see the header's requirements).
+bool cache_tma_geometry(const b200_cache_desc* cache, int tile_tokens, CacheTmaGeometry* geo,
+                        std::string* why);
+
+// Encodes (or returns a cached copy of) the tensor map of one cache tensor.
+int encode_cache_tensor_map(const b200_cache_desc* cache, const void* base,
+                            const CacheTmaGeometry& geo, CUtensorMap* out);
+
+inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace b200

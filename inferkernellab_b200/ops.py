@@ -1,0 +1,441 @@
+"""Reference-compatible operators backed by the sm_100a kernels.
+
+Each function keeps the signature, argument meaning, validation order and
+exception types of the reference wrapper it replaces, so it can be registered
+as a backend next to ``paged_reference`` / ``paged_sdpa`` / ``triton_paged``:
+
+=====================================  ==========================================================
+this module                            reference (``src/inferkernellab/``)
+=====================================  ==========================================================
+``paged_decode_attention``             ``triton_ops.paged_decode_attention_triton`` (:404-478) and
+                                       ``..._triton_grouped`` (:481-610)
+``append_kv``                          ``append.append_kv_triton`` (:69-106)
+``paged_prefill_attention``            ``attention.paged_prefill_attention_sdpa`` (:230-321)
+``paged_prefill_attention_varlen``     (new) packed ``[sum T, Hq, D]`` form over ``cu_seqlens``
+``build_slot_mapping``                 (new) device form of ``PagedKVCache.slot_mapping`` for a batch
+=====================================  ==========================================================
+
+All launches go on torch's current CUDA stream through the C ABI in
+``_lib``; no torch type crosses it.  There is no CPU or torch fallback: a
+missing library, a non-CUDA tensor or an unsupported shape raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+
+_DTYPE_CODE = {torch.float16: _lib.B200_F16, torch.bfloat16: _lib.B200_BF16}
+_INDEX_CODE = {torch.int32: _lib.B200_I32, torch.int64: _lib.B200_I64}
+
+
+def b200_available() -> bool:
+    """True when a CUDA device is visible and the library can be loaded."""
+    if not torch.cuda.is_available():
+        return False
+    try:
+        _lib.load()
+    except (OSError, RuntimeError):
+        return False
+    return True
+
+
+def _stream_ptr(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _cache_desc(cache) -> _lib.CacheDesc:
+    layout = cache.layout
+    k, v = cache.k, cache.v
+    if k.dtype not in _DTYPE_CODE:
+        raise ValueError("the B200 kernels support float16 and bfloat16 caches")
+    if not (k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("cache K/V storage must be contiguous")
+    if k.device.type != "cuda":
+        raise ValueError("the cache must live on a CUDA device")
+    return _lib.CacheDesc(k.data_ptr(), v.data_ptr(), layout.num_layers, layout.num_blocks,
+                          layout.block_size, layout.num_kv_heads, layout.head_dim,
+                          _DTYPE_CODE[k.dtype])
+
+
+# ----------------------------------------------------------------- workspace
+
+class _Workspaces:
+    """Per-(device, stream) decode workspace, zero-filled once and kept.
+
+    The decode kernel's split counters return to zero at the end of every
+    launch, so a workspace is only zeroed when it is (re)allocated.  Keeping one
+    per stream means launches on different streams never share counters.
+    """
+
+    def __init__(self):
+        self._lock = threading.Lock()
+        self._buffers: dict[tuple[int, int], torch.Tensor] = {}
+
+    def get(self, device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+        key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
+        with self._lock:
+            buf = self._buffers.get(key)
+            if buf is None or buf.numel() < nbytes:
+                size = max(nbytes, 1 << 20)
+                if buf is not None:
+                    size = max(size, 2 * buf.numel())
+                buf = torch.zeros(size, dtype=torch.uint8, device=device)
+                self._buffers[key] = buf
+            return buf
+
+    def reset(self) -> None:
+        with self._lock:
+            for buf in self._buffers.values():
+                buf.zero_()
+
+    def error_words(self):
+        with self._lock:
+            return list(self._buffers.values())
+
+
+_WORKSPACES = _Workspaces()
+
+
+class _ErrorWords:
+    """One zeroed device word per device for the append/prefill/metadata kernels."""
+
+    def __init__(self):
+        self._lock = threading.Lock()
+        self._words: dict[int, torch.Tensor] = {}
+
+    def get(self, device: torch.device) -> torch.Tensor:
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        with self._lock:
+            word = self._words.get(index)
+            if word is None:
+                word = torch.zeros(64, dtype=torch.int32, device=torch.device("cuda", index))
+                self._words[index] = word
+            return word
+
+    def all(self):
+        with self._lock:
+            return list(self._words.values())
+
+
+_ERROR_WORDS = _ErrorWords()
+
+
+def _read_word(word: torch.Tensor, clear: bool) -> int:
+    value = ctypes.c_uint32(0)
+    _lib.check(_lib.load().b200_read_error_word(ctypes.c_void_p(word.data_ptr()),
+                                                ctypes.byref(value), int(clear),
+                                                _stream_ptr(word.device)))
+    return int(value.value)
+
+
+def check_device_errors(clear: bool = True) -> int:
+    """Synchronise and return the OR of every decode workspace's device error word.
+
+    Non-zero bits are ``_lib.DEVERR_*``.  A bounded-wait timeout (bits 1, 2, 16)
+    means the affected outputs are not valid; in that case the workspaces are
+    zeroed again so that stale split counters cannot leak into later calls.
+    """
+    value = 0
+    for buf in _WORKSPACES.error_words() + _ERROR_WORDS.all():
+        value |= _read_word(buf, clear)
+    if value & (_lib.DEVERR_WAIT_FULL | _lib.DEVERR_WAIT_EMPTY | _lib.DEVERR_DRAIN):
+        _WORKSPACES.reset()
+    return value
+
+
+# ------------------------------------------------------------------- decode
+
+def _as_index_tensor(values, device: torch.device) -> torch.Tensor:
+    if isinstance(values, list):
+        return torch.tensor(values, dtype=torch.int32, device=device)
+    return values
+
+
+def paged_decode_attention(query: torch.Tensor, cache, block_tables, context_lens, scale=None,
+                           layer: int = 0, *, validate_inputs: bool = True,
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+    """Paged decode attention on the sm_100a split-KV kernel.
+
+    Drop-in for ``paged_decode_attention_triton(query, cache, block_tables,
+    context_lens, scale=None, layer=0, *, validate_inputs=True)`` (reference
+    ``triton_ops.py:404-478``); MHA, GQA and MQA all take the same kernel, so it
+    also replaces ``paged_decode_attention_triton_grouped``.  ``out``
+    (optional, ``[B, Hq, D]``) receives the result instead of a new tensor.
+    """
+    if query.ndim != 3 or query.device.type != "cuda":
+        raise ValueError("query must be a CUDA tensor with shape [B,H,D]")
+    if query.shape[0] <= 0 or query.shape[1] <= 0 or query.shape[2] <= 0:
+        raise ValueError("query dimensions must be positive")
+    if query.stride(-1) != 1:
+        raise ValueError("query must be contiguous in the head_dim dimension")
+    block_tables = _as_index_tensor(block_tables, query.device)
+    context_lens = _as_index_tensor(context_lens, query.device)
+    layout = cache.layout
+    if not 0 <= layer < layout.num_layers:
+        raise IndexError("layer is out of range")
+    if query.shape[-1] != layout.head_dim:
+        raise ValueError("query head_dim does not match cache layout")
+    if query.shape[1] % layout.num_kv_heads != 0:
+        raise ValueError("num_heads must be divisible by num_kv_heads")
+    if query.dtype != cache.k.dtype or query.device != cache.k.device:
+        raise ValueError("query and cache must have the same dtype and device")
+    if block_tables.ndim != 2 or block_tables.shape[0] != query.shape[0]:
+        raise ValueError("block_tables must have shape [B, max_blocks]")
+    if context_lens.ndim != 1 or context_lens.shape[0] != query.shape[0]:
+        raise ValueError("context_lens must have shape [B]")
+    if block_tables.device != query.device or context_lens.device != query.device:
+        raise ValueError("block_tables and context_lens must be on the query device")
+    if block_tables.dtype not in _INDEX_CODE:
+        raise ValueError("block_tables must use int32 or int64")
+    if context_lens.dtype not in _INDEX_CODE:
+        raise ValueError("context_lens must use int32 or int64")
+    if block_tables.shape[1] <= 0:
+        raise ValueError("block_tables must contain at least one logical block")
+    lib = _lib.load()
+    stream = _stream_ptr(query.device)
+    if block_tables.stride(-1) != 1:
+        block_tables = block_tables.contiguous()
+    if not context_lens.is_contiguous():
+        context_lens = context_lens.contiguous()
+    if validate_inputs:
+        flags = torch.empty(3, dtype=torch.int32, device=query.device)
+        _lib.check(lib.b200_validate_decode_metadata(
+            block_tables.data_ptr(), _INDEX_CODE[block_tables.dtype], block_tables.stride(0),
+            block_tables.shape[1], context_lens.data_ptr(), _INDEX_CODE[context_lens.dtype],
+            query.shape[0], layout.block_size, layout.num_blocks, flags.data_ptr(), stream))
+        bad_len, too_long, bad_block = (bool(x) for x in flags.tolist())
+        if bad_len:
+            raise ValueError("context lengths must be positive")
+        if too_long:
+            raise ValueError("context length exceeds block table capacity")
+        if bad_block:
+            raise ValueError("block table contains an invalid physical block id")
+    if query.stride(0) % 2 or query.stride(1) % 2 or query.data_ptr() % 4:
+        query = query.contiguous()
+    if out is None:
+        out = torch.empty(query.shape, dtype=query.dtype, device=query.device)
+    elif out.shape != query.shape or out.dtype != query.dtype or out.stride(-1) != 1:
+        raise ValueError("out must match the query shape and dtype")
+    desc = _cache_desc(cache)
+    args = _lib.DecodeArgs(
+        query.shape[0], query.shape[1], block_tables.shape[1], layer,
+        query.stride(0), query.stride(1), out.stride(0), out.stride(1), block_tables.stride(0),
+        _INDEX_CODE[block_tables.dtype], _INDEX_CODE[context_lens.dtype],
+        float(scale) if scale is not None else layout.head_dim ** -0.5)
+    need = lib.b200_paged_decode_workspace_bytes(ctypes.byref(desc), ctypes.byref(args))
+    if need == 0:
+        _lib.check(_lib.B200_ERR_INVALID if _lib.last_error() else _lib.B200_ERR_CUDA)
+    ws = _WORKSPACES.get(query.device, stream.value or 0, need)
+    _lib.check(lib.b200_paged_decode(ctypes.byref(desc), ctypes.byref(args), query.data_ptr(),
+                                     block_tables.data_ptr(), context_lens.data_ptr(),
+                                     out.data_ptr(), ws.data_ptr(), ws.numel(), stream))
+    return out
+
+
+# -------------------------------------------------------------------- append
+
+def append_kv(key: torch.Tensor, value: torch.Tensor, cache, slots: torch.Tensor,
+              layer: int = 0) -> None:
+    """Scatter ``[T, Hkv, D]`` K/V into ``cache`` at physical ``slots``, bit-exact.
+
+    Drop-in for ``append_kv_triton(key, value, cache, slots, layer=0)``
+    (reference ``append.py:69-106``); ``slots`` may be int32 or int64.  Negative
+    slots are skipped (padding).
+    """
+    if key.shape != value.shape or key.ndim != 3:
+        raise ValueError("key/value must have shape [T, Hkv, D]")
+    if key.device.type != "cuda" or slots.device != key.device or value.device != key.device:
+        raise ValueError("key/value/slots must be on the same CUDA device")
+    layout = cache.layout
+    if tuple(key.shape[1:]) != (layout.num_kv_heads, layout.head_dim):
+        raise ValueError("key/value shape does not match cache layout")
+    if slots.numel() != key.shape[0]:
+        raise ValueError("slots and key/value token counts must match")
+    if not 0 <= layer < layout.num_layers:
+        raise IndexError("layer is out of range")
+    if key.dtype != cache.k.dtype or value.dtype != cache.k.dtype:
+        raise ValueError("key/value must have the cache dtype")
+    if slots.dtype not in _INDEX_CODE:
+        raise ValueError("slots must use int32 or int64")
+    if key.shape[0] == 0:
+        return
+    if key.stride(-1) != 1:
+        key = key.contiguous()
+    if value.stride(-1) != 1:
+        value = value.contiguous()
+    slots = slots.reshape(-1)
+    if not slots.is_contiguous():
+        slots = slots.contiguous()
+    desc = _cache_desc(cache)
+    _lib.check(_lib.load().b200_append_kv(
+        ctypes.byref(desc), layer, key.data_ptr(), value.data_ptr(), key.shape[0],
+        key.stride(0), key.stride(1), value.stride(0), value.stride(1), slots.data_ptr(),
+        _INDEX_CODE[slots.dtype], _ERROR_WORDS.get(key.device).data_ptr(),
+        _stream_ptr(key.device)))
+
+
+# ------------------------------------------------------------------- prefill
+
+def _prefill_index(values, device) -> tuple[torch.Tensor, list[int]]:
+    if isinstance(values, torch.Tensor):
+        host = values.detach().cpu().tolist()
+    else:
+        host = [int(v) for v in values]
+    return torch.tensor(host, dtype=torch.int64, device=device), host
+
+
+def paged_prefill_attention(query: torch.Tensor, cache, block_tables, query_starts, context_lens,
+                            *, scale=None, layer: int = 0) -> torch.Tensor:
+    """Ragged causal prefill over the paged cache, padded ``[B, Hq, T, D]`` form.
+
+    Drop-in for ``paged_prefill_attention_sdpa`` (reference ``attention.py:230-321``):
+    row ``b`` holds query positions ``query_starts[b] .. context_lens[b]-1``;
+    padded rows attend key 0 only, as in the reference mask.  The cache must
+    already hold every key of each range.
+    """
+    if query.ndim != 4:
+        raise ValueError("query must be [B,H,T,D]")
+    batch, num_heads, query_width, head_dim = query.shape
+    layout = cache.layout
+    if head_dim != layout.head_dim:
+        raise ValueError("query head_dim does not match cache")
+    if num_heads % layout.num_kv_heads != 0:
+        raise ValueError("num_heads must be divisible by num_kv_heads")
+    if query.device != cache.k.device or query.device.type != "cuda":
+        raise ValueError("query and cache must be on the same device")
+    starts_t, starts = _prefill_index(query_starts, query.device)
+    ends_t, ends = _prefill_index(context_lens, query.device)
+    if len(starts) != batch or len(ends) != batch:
+        raise ValueError("query_starts and context_lens must have one entry per query batch")
+    lengths = [e - s for s, e in zip(starts, ends)]
+    if any(s < 0 or n <= 0 for s, n in zip(starts, lengths)):
+        raise ValueError("prefill ranges must be non-empty and non-negative")
+    if max(lengths) > query_width:
+        raise ValueError("query width is smaller than a prefill range")
+    if not 0 <= layer < layout.num_layers:
+        raise IndexError("layer is out of range")
+    if isinstance(block_tables, torch.Tensor):
+        tables = block_tables.to(device=query.device)
+    else:
+        tables = torch.as_tensor(block_tables, dtype=torch.int64, device=query.device)
+    if tables.ndim != 2 or tables.shape[0] != batch:
+        raise ValueError("block_tables must have one row per query batch")
+    if tables.dtype not in _INDEX_CODE:
+        tables = tables.to(torch.int64)
+    if -(-max(ends) // layout.block_size) > tables.shape[1]:
+        raise ValueError("context length exceeds block table capacity")
+    if query.dtype != cache.k.dtype:
+        raise ValueError("query and cache must have the same dtype")
+    if query.stride(-1) != 1 or query.stride(0) % 2 or query.stride(1) % 2 or query.stride(2) % 2:
+        query = query.contiguous()
+    tables = tables.contiguous()
+    out = torch.empty(query.shape, dtype=query.dtype, device=query.device)
+    desc = _cache_desc(cache)
+    args = _lib.PrefillArgs(
+        batch, num_heads, tables.shape[1], layer, 0, query_width, 0,
+        query.stride(0), query.stride(1), query.stride(2),
+        out.stride(0), out.stride(1), out.stride(2), tables.stride(0),
+        _INDEX_CODE[tables.dtype], _lib.B200_I64,
+        float(scale) if scale is not None else head_dim ** -0.5)
+    _lib.check(_lib.load().b200_paged_prefill(
+        ctypes.byref(desc), ctypes.byref(args), query.data_ptr(), tables.data_ptr(),
+        starts_t.data_ptr(), ends_t.data_ptr(), None, out.data_ptr(),
+        _ERROR_WORDS.get(query.device).data_ptr(), _stream_ptr(query.device)))
+    return out
+
+
+def paged_prefill_attention_varlen(query: torch.Tensor, cache, block_tables: torch.Tensor,
+                                   cu_seqlens_q: torch.Tensor, query_starts: torch.Tensor,
+                                   context_lens: torch.Tensor, *, scale=None, layer: int = 0,
+                                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """Packed ragged causal prefill: ``query`` ``[sum T, Hq, D]``, no padding.
+
+    Sequence ``b`` owns rows ``cu_seqlens_q[b] .. cu_seqlens_q[b+1]-1`` which
+    are the query tokens of logical positions ``query_starts[b] ..
+    context_lens[b]-1``.  All metadata stays on the device (no host sync);
+    ``cu_seqlens_q`` is int32, ``query_starts``/``context_lens`` int32 or int64.
+    """
+    if query.ndim != 3 or query.device.type != "cuda":
+        raise ValueError("query must be a CUDA tensor with shape [T,H,D]")
+    total, num_heads, head_dim = query.shape
+    layout = cache.layout
+    if head_dim != layout.head_dim:
+        raise ValueError("query head_dim does not match cache")
+    if num_heads % layout.num_kv_heads != 0:
+        raise ValueError("num_heads must be divisible by num_kv_heads")
+    if query.dtype != cache.k.dtype or query.device != cache.k.device:
+        raise ValueError("query and cache must have the same dtype and device")
+    if not 0 <= layer < layout.num_layers:
+        raise IndexError("layer is out of range")
+    if cu_seqlens_q.dtype != torch.int32 or cu_seqlens_q.ndim != 1:
+        raise ValueError("cu_seqlens_q must be a 1-D int32 tensor")
+    batch = cu_seqlens_q.shape[0] - 1
+    if batch <= 0 or query_starts.shape != (batch,) or context_lens.shape != (batch,):
+        raise ValueError("query_starts and context_lens must have one entry per sequence")
+    if query_starts.dtype != context_lens.dtype or query_starts.dtype not in _INDEX_CODE:
+        raise ValueError("query_starts and context_lens must share an int32/int64 dtype")
+    if block_tables.ndim != 2 or block_tables.shape[0] != batch:
+        raise ValueError("block_tables must have one row per sequence")
+    if block_tables.dtype not in _INDEX_CODE:
+        raise ValueError("block_tables must use int32 or int64")
+    if query.stride(-1) != 1 or query.stride(0) % 2 or query.stride(1) % 2:
+        query = query.contiguous()
+    block_tables = block_tables.contiguous()
+    if out is None:
+        out = torch.empty(query.shape, dtype=query.dtype, device=query.device)
+    desc = _cache_desc(cache)
+    args = _lib.PrefillArgs(
+        batch, num_heads, block_tables.shape[1], layer, 1, 0, total,
+        0, query.stride(1), query.stride(0), 0, out.stride(1), out.stride(0),
+        block_tables.stride(0), _INDEX_CODE[block_tables.dtype], _INDEX_CODE[query_starts.dtype],
+        float(scale) if scale is not None else head_dim ** -0.5)
+    _lib.check(_lib.load().b200_paged_prefill(
+        ctypes.byref(desc), ctypes.byref(args), query.data_ptr(), block_tables.data_ptr(),
+        query_starts.contiguous().data_ptr(), context_lens.contiguous().data_ptr(),
+        cu_seqlens_q.contiguous().data_ptr(), out.data_ptr(),
+        _ERROR_WORDS.get(query.device).data_ptr(), _stream_ptr(query.device)))
+    return out
+
+
+# ------------------------------------------------------------------ metadata
+
+def build_slot_mapping(block_tables: torch.Tensor, starts: torch.Tensor, ends: torch.Tensor, *,
+                       block_size: int, num_blocks: int, total_tokens: int,
+                       slots_dtype: torch.dtype = torch.int32,
+                       with_cu_seqlens: bool = True):
+    """Device-built slots of every scheduled token of a batch, plus ``cu_seqlens``.
+
+    For each sequence ``b`` and position ``p`` in ``starts[b] .. ends[b]-1``:
+    ``slot = block_tables[b, p // block_size] * block_size + p % block_size``,
+    packed in sequence order -- the same numbers the reference's per-request
+    ``PagedKVCache.slot_mapping`` + ``torch.cat`` produce (``cache.py:113-129``,
+    ``decode.py:330-335``), built in one launch from device-resident tables.
+    Positions past the table or with an out-of-range block id get ``-1``.
+    Returns ``(slots [total_tokens], cu_seqlens int32 [B+1] or None)``.
+    """
+    if block_tables.ndim != 2 or block_tables.device.type != "cuda":
+        raise ValueError("block_tables must be a 2-D CUDA tensor")
+    batch = block_tables.shape[0]
+    if starts.shape != (batch,) or ends.shape != (batch,):
+        raise ValueError("starts and ends must have one entry per table row")
+    if starts.dtype != ends.dtype or starts.dtype not in _INDEX_CODE:
+        raise ValueError("starts and ends must share an int32/int64 dtype")
+    if block_tables.dtype not in _INDEX_CODE or slots_dtype not in _INDEX_CODE:
+        raise ValueError("block_tables and slots must use int32 or int64")
+    block_tables = block_tables.contiguous() if block_tables.stride(-1) != 1 else block_tables
+    device = block_tables.device
+    slots = torch.empty(total_tokens, dtype=slots_dtype, device=device)
+    cu = torch.empty(batch + 1, dtype=torch.int32, device=device) if with_cu_seqlens else None
+    _lib.check(_lib.load().b200_build_slot_mapping(
+        block_tables.data_ptr(), _INDEX_CODE[block_tables.dtype], block_tables.stride(0),
+        block_tables.shape[1], starts.contiguous().data_ptr(), ends.contiguous().data_ptr(),
+        _INDEX_CODE[starts.dtype], batch, block_size, num_blocks,
+        slots.data_ptr() if total_tokens else None, _INDEX_CODE[slots_dtype], total_tokens,
+        cu.data_ptr() if cu is not None else None, _ERROR_WORDS.get(device).data_ptr(),
+        _stream_ptr(device)))
+    return slots, cu

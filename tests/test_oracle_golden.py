@@ -1,0 +1,77 @@
+"""Pin the numpy oracle against the reference's own outputs (tests/golden/*.npz).
+
+The fixtures were produced by importing the reference project itself
+(tests/golden/make_golden.py); these tests need no GPU.
+"""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def test_slot_mapping_matches_reference_vectors():
+    data = np.load(GOLDEN / "slot_mapping.npz")
+    for name in data["cases"]:
+        got = oracle.slot_mapping(data[f"{name}_table"].tolist(), int(data[f"{name}_start"]),
+                                  int(data[f"{name}_length"]), int(data[f"{name}_block_size"]),
+                                  int(data[f"{name}_num_blocks"]))
+        np.testing.assert_array_equal(got, data[f"{name}_slots"])
+    # The reference's own literal (tests/test_cache.py:8-12).
+    assert oracle.slot_mapping([6, 2, 5], 2, 6, 4, 8).tolist() == [26, 27, 8, 9, 10, 11]
+
+
+def test_slot_mapping_errors_match_reference():
+    with pytest.raises(ValueError, match="invalid physical block"):
+        oracle.slot_mapping([-1], 0, 1, 4, 4)
+    with pytest.raises(ValueError, match="shorter"):
+        oracle.slot_mapping([2], 4, 1, 4, 4)
+    with pytest.raises(ValueError, match="non-negative"):
+        oracle.slot_mapping([0], -1, 1, 4, 4)
+
+
+@pytest.mark.parametrize("path", sorted(GOLDEN.glob("decode_*.npz")), ids=lambda p: p.stem)
+def test_decode_oracle_matches_reference(path):
+    d = np.load(path)
+    kind = str(d["kind"])
+    scale = None if np.isnan(d["scale"]) else float(d["scale"])
+    got = oracle.paged_decode_attention(d["query"], d["k"], d["v"], kind, d["block_tables"].tolist(),
+                                        d["context_lens"].tolist(), scale=scale, layer=int(d["layer"]))
+    np.testing.assert_allclose(got, d["out_f32"], atol=2e-6, rtol=2e-5)
+    # The reference's native-dtype output is the fp32 result rounded once.
+    native = oracle.to_f32(d["out_native"], kind)
+    tol = 1e-2 if kind == "bf16" else 2e-3
+    np.testing.assert_allclose(got, native, atol=tol, rtol=tol)
+
+
+@pytest.mark.parametrize("path", sorted(GOLDEN.glob("prefill_*.npz")), ids=lambda p: p.stem)
+def test_prefill_oracle_matches_reference(path):
+    d = np.load(path)
+    got = oracle.paged_prefill_attention(d["query"], d["k"], d["v"], str(d["kind"]),
+                                         d["block_tables"].tolist(), d["query_starts"].tolist(),
+                                         d["context_lens"].tolist())
+    # Every row, padded rows included (they attend key 0 in both).
+    np.testing.assert_allclose(got, d["out_f32"], atol=2e-6, rtol=2e-5)
+
+
+def test_append_oracle_matches_reference():
+    d = np.load(GOLDEN / "append.npz")
+    k = np.zeros_like(d["k_after"])
+    v = np.zeros_like(d["v_after"])
+    oracle.write_slots(k, v, int(d["layer"]), d["slots"], d["key"], d["value"])
+    np.testing.assert_array_equal(k.view(np.uint16), d["k_after"].view(np.uint16))
+    np.testing.assert_array_equal(v.view(np.uint16), d["v_after"].view(np.uint16))
+
+
+def test_bf16_round_trip_is_exact_and_rounds_to_nearest_even():
+    bits = np.arange(0, 1 << 16, 7, dtype=np.uint16)
+    f = oracle.bf16_bits_to_f32(bits)
+    finite = np.isfinite(f)
+    np.testing.assert_array_equal(oracle.f32_to_bf16_bits(f[finite]), bits[finite])
+    # 1 + 2^-8 is exactly between two bf16 values: ties go to the even mantissa (1.0).
+    assert oracle.f32_to_bf16_bits(np.array([1.0 + 2 ** -8], np.float32))[0] == 0x3F80
+    assert oracle.f32_to_bf16_bits(np.array([1.0 + 3 * 2 ** -8], np.float32))[0] == 0x3F82
