@@ -440,17 +440,23 @@ struct WorkspaceLayout {
   size_t err_off, counters_off, lse_off, o_off, total;
 };
 
+// [0, 256): device error word.  Then the split partials, whose size depends only
+// on (grid, group, head_dim) -- fixed for a model on a device -- and last the
+// per-segment counters (num_seqs * kv_heads).  Counters go last so that a change
+// of batch size never moves them onto bytes that held partials: counters past
+// the previous batch were never written, the others were reset by the kernel.
 static WorkspaceLayout workspace_layout(int num_seqs, int hkv, int group, int head_dim, int grid) {
+  auto round256 = [](size_t x) { return (x + 255) / 256 * 256; };
   WorkspaceLayout w;
   size_t off = 0;
   w.err_off = off;
   off += 256;
-  w.counters_off = off;
-  off += ((static_cast<size_t>(num_seqs) * hkv * 4 + 255) / 256) * 256;
   w.lse_off = off;
-  off += ((static_cast<size_t>(2) * grid * group * 4 + 255) / 256) * 256;
+  off += round256(static_cast<size_t>(2) * grid * group * 4);
   w.o_off = off;
-  off += static_cast<size_t>(2) * grid * group * head_dim * 4;
+  off += round256(static_cast<size_t>(2) * grid * group * head_dim * 4);
+  w.counters_off = off;
+  off += round256(static_cast<size_t>(num_seqs) * hkv * 4);
   w.total = off;
   return w;
 }
@@ -476,7 +482,13 @@ static int launch_decode_t(const CUtensorMap& kmap, const CUtensorMap& vmap,
   if (per_sm < 1)
     return set_error(B200_ERR_UNSUPPORTED, "decode kernel does not fit on an SM (shared memory)");
   const int grid = num_sms * per_sm;
-  *grid_out = grid;
+  // The workspace is sized for the largest grid of this instantiation (the
+  // occupancy at batch size 1), so its layout does not move with the batch.
+  const int smem_min = decode_smem_layout<D, MT>(p.group, 1).total + 1024;
+  int per_sm_max = 0;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_max, kern, kDecThreads, smem_min);
+  if (err != cudaSuccess) return cuda_status(err, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  *grid_out = num_sms * (per_sm_max > per_sm ? per_sm_max : per_sm);
   if (dry_run) return B200_OK;
   kern<<<grid, kDecThreads, smem, stream>>>(kmap, vmap, p);
   return cuda_status(cudaGetLastError(), "paged_decode_kernel launch");

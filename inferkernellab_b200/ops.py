@@ -75,8 +75,16 @@ class _Workspaces:
     def __init__(self):
         self._lock = threading.Lock()
         self._buffers: dict[tuple[int, int], torch.Tensor] = {}
+        self._shape_class: dict[tuple[int, int], tuple] = {}
 
-    def get(self, device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    def get(self, device: torch.device, stream: int, nbytes: int,
+            shape_class: tuple = ()) -> torch.Tensor:
+        """Workspace of at least ``nbytes``; re-zeroed when ``shape_class`` changes.
+
+        ``shape_class`` = (group, head_dim, dtype): the partial-region size
+        depends on it, so a change could leave old partial bytes under the
+        split counters (see the header's workspace contract).
+        """
         key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
         with self._lock:
             buf = self._buffers.get(key)
@@ -86,6 +94,9 @@ class _Workspaces:
                     size = max(size, 2 * buf.numel())
                 buf = torch.zeros(size, dtype=torch.uint8, device=device)
                 self._buffers[key] = buf
+            elif self._shape_class.get(key) != shape_class:
+                buf.zero_()
+            self._shape_class[key] = shape_class
             return buf
 
     def reset(self) -> None:
@@ -230,7 +241,8 @@ def paged_decode_attention(query: torch.Tensor, cache, block_tables, context_len
     need = lib.b200_paged_decode_workspace_bytes(ctypes.byref(desc), ctypes.byref(args))
     if need == 0:
         _lib.check(_lib.B200_ERR_INVALID if _lib.last_error() else _lib.B200_ERR_CUDA)
-    ws = _WORKSPACES.get(query.device, stream.value or 0, need)
+    ws = _WORKSPACES.get(query.device, stream.value or 0, need,
+                         (query.shape[1] // layout.num_kv_heads, layout.head_dim, query.dtype))
     _lib.check(lib.b200_paged_decode(ctypes.byref(desc), ctypes.byref(args), query.data_ptr(),
                                      block_tables.data_ptr(), context_lens.data_ptr(),
                                      out.data_ptr(), ws.data_ptr(), ws.numel(), stream))

@@ -167,3 +167,23 @@ def test_decode_on_side_stream():
                                      validate_inputs=False)
     torch.cuda.current_stream().wait_stream(side)
     assert_close(out, case.oracle(), torch.float16, "side stream")
+
+
+def test_decode_workspace_survives_changing_batch_and_shape_class():
+    """One workspace, calls with growing/shrinking batches and different head
+    groupings in a row: split counters must never see stale partial bytes."""
+    plan = [
+        (6, 32, 8, 128, [3000, 17, 2048, 1, 900, 4095]),
+        (16, 32, 8, 128, [8192, 1] + [500 + 431 * i for i in range(14)]),
+        (3, 32, 8, 128, [7000, 64, 65]),
+        (5, 32, 1, 64, [600, 5, 1200, 33, 2]),
+        (40, 32, 8, 128, [97 * (i + 1) for i in range(40)]),
+        (2, 32, 8, 128, [5000, 4999]),
+    ]
+    for i, (batch, hq, hkv, dim, lens) in enumerate(plan):
+        case = DecodeCase(batch=batch, num_heads=hq, num_kv_heads=hkv, head_dim=dim,
+                          block_size=16, lens=lens, dtype=torch.bfloat16, seed=100 + i)
+        out = paged_decode_attention(case.query, case.cache, case.tables, case.lens,
+                                     validate_inputs=False)
+        assert_close(out, case.oracle(), torch.bfloat16, f"plan step {i}")
+    assert check_device_errors() == 0
