@@ -113,6 +113,37 @@ B200_API int b200_paged_decode(const b200_cache_desc* cache, const b200_decode_a
                       const void* block_tables, const void* context_lens, void* out,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------- allocation-free decode
+ * No counterpart in the reference: an addition of this library.
+ *
+ * Same computation and arguments as b200_paged_decode, minus the workspace.
+ * It is for callers that cannot allocate device memory while attention runs --
+ * a plugin or custom operator executing inside a host framework that owns all
+ * buffers and forbids cudaMalloc at that point (it would also synchronise the
+ * device), or code held to a fixed memory budget.  The caller still passes the
+ * query, the metadata and the output buffer; the split-KV scratch comes from a
+ * static device array of b200_paged_decode_noalloc_scratch_bytes() (8 MiB) that
+ * every GPU loading the library holds until the process exits.
+ *
+ *  - Allocates nothing: no cudaMalloc / cudaFree, no allocating library call.
+ *  - Shapes whose split scratch would exceed 8 MiB are rejected with
+ *    B200_ERR_WORKSPACE and a message (for example 64 query heads per KV head
+ *    at head_dim 128); use b200_paged_decode with a workspace for those.
+ *  - The first call on a device, with that device current, resolves the
+ *    array's device address (cudaGetSymbolAddress); make that first call
+ *    before any stream capture.
+ *  - All calls share the one array and it keeps the last call's contents:
+ *    each call zeroes the error word and split counters (two cudaMemsetAsync
+ *    on `stream`) before its launch.  Calls whose executions overlap on the
+ *    GPU (different streams without ordering) race on the array.
+ */
+B200_API int b200_paged_decode_noalloc(const b200_cache_desc* cache, const b200_decode_args* args,
+                                       const void* query, const void* block_tables,
+                                       const void* context_lens, void* out, void* stream);
+
+/* Size in bytes of the static scratch array used by b200_paged_decode_noalloc. */
+B200_API size_t b200_paged_decode_noalloc_scratch_bytes(void);
+
 /* ------------------------------------------------------------------ append
  * Reshape-and-cache: cache[layer, slot/BS, slot%BS, h, :] = key[t, h, :] (and V)
  * for every token t, bit-exact.  Replaces the reference's append_kv_triton and

@@ -37,6 +37,8 @@ DEVERR_DRAIN = 16
 EXPORTED_SYMBOLS = (
     "b200_paged_decode_workspace_bytes",
     "b200_paged_decode",
+    "b200_paged_decode_noalloc",
+    "b200_paged_decode_noalloc_scratch_bytes",
     "b200_append_kv",
     "b200_paged_prefill",
     "b200_build_slot_mapping",
@@ -107,6 +109,10 @@ _PROTOTYPES = {
                                                             ctypes.POINTER(DecodeArgs)]),
     "b200_paged_decode": (ctypes.c_int, [ctypes.POINTER(CacheDesc), ctypes.POINTER(DecodeArgs), _vp,
                                          _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "b200_paged_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(CacheDesc),
+                                                 ctypes.POINTER(DecodeArgs), _vp, _vp, _vp, _vp,
+                                                 _vp]),
+    "b200_paged_decode_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "b200_append_kv": (ctypes.c_int, [ctypes.POINTER(CacheDesc), _i32, _vp, _vp, _i64, _i64, _i64,
                                       _i64, _i64, _vp, _i32, _vp, _vp]),
     "b200_paged_prefill": (ctypes.c_int, [ctypes.POINTER(CacheDesc), ctypes.POINTER(PrefillArgs),

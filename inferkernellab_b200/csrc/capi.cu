@@ -53,6 +53,19 @@ int b200_paged_decode(const b200_cache_desc* cache, const b200_decode_args* args
   });
 }
 
+int b200_paged_decode_noalloc(const b200_cache_desc* cache, const b200_decode_args* args,
+                              const void* query, const void* block_tables,
+                              const void* context_lens, void* out, void* stream) {
+  return guarded([&] {
+    return b200::launch_paged_decode_noalloc(cache, args, query, block_tables, context_lens, out,
+                                             as_stream(stream));
+  });
+}
+
+size_t b200_paged_decode_noalloc_scratch_bytes(void) {
+  return b200::decode_noalloc_scratch_bytes();
+}
+
 int b200_append_kv(const b200_cache_desc* cache, int32_t layer, const void* key, const void* value,
                    int64_t num_tokens, int64_t key_stride_token, int64_t key_stride_head,
                    int64_t value_stride_token, int64_t value_stride_head, const void* slots,

@@ -28,6 +28,8 @@
 // unwritten cache slots never reaches the output.
 #include <math.h>
 
+#include <mutex>
+
 #include "../../include/b200_paged_attn.h"
 #include "attn_core.cuh"
 #include "common.cuh"
@@ -631,6 +633,85 @@ int launch_paged_decode(const b200_cache_desc* c, const b200_decode_args* a, con
   return c->dtype == B200_BF16
              ? dispatch_d<BF16>(c->head_dim, mt, kmap, vmap, p, info.num_sms, &grid, false, stream)
              : dispatch_d<Half>(c->head_dim, mt, kmap, vmap, p, info.num_sms, &grid, false, stream);
+}
+
+// ------------------------------------------------------ allocation-free entry
+//
+// Some callers of this library cannot allocate device memory when they run
+// attention: a plugin or custom operator inside a host framework's execute
+// step (the host owns every buffer and forbids cudaMalloc there, which would
+// also synchronise the device), or code running under a fixed memory budget.
+// They pass only inputs and outputs; the split-KV scratch of the decode kernel
+// then comes from this file-scope device array instead of a caller workspace.
+//
+// The array is kDecodeNoAllocScratchBytes (8 MiB) on every GPU that loads the
+// library, kept until the process exits.  All calls share it and it keeps the
+// last call's contents, so each call zeroes the parts that must start at zero
+// (the error word and the split counters) before its launch, and calls whose
+// executions overlap on the GPU (different streams, no ordering) race on it.
+constexpr size_t kDecodeNoAllocScratchBytes = static_cast<size_t>(8) << 20;
+static __device__ __align__(256) uint8_t g_decode_noalloc_scratch[kDecodeNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};  // device address of the array, per device
+}  // namespace
+
+// Host code may not use the array's name as a device address; resolve it once
+// per device, with that device current.
+static int noalloc_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_status(err, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return set_error(B200_ERR_UNSUPPORTED, "device index >= 64");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_decode_noalloc_scratch);
+    if (err != cudaSuccess) return cuda_status(err, "cudaGetSymbolAddress(decode scratch)");
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return B200_OK;
+}
+
+size_t decode_noalloc_scratch_bytes() { return kDecodeNoAllocScratchBytes; }
+
+int launch_paged_decode_noalloc(const b200_cache_desc* c, const b200_decode_args* a,
+                                const void* query, const void* block_tables,
+                                const void* context_lens, void* out, cudaStream_t stream) {
+  int rc = check_decode_args(c, a);
+  if (rc != B200_OK) return rc;
+  DeviceInfo info;
+  rc = current_device_info(&info);
+  if (rc != B200_OK) return rc;
+  const int group = a->num_q_heads / c->num_kv_heads;
+  const int mt = group <= 16 ? 1 : (group <= 32 ? 2 : 4);
+  CUtensorMap unused;
+  DecodeParams probe{};
+  probe.group = group;
+  probe.num_seqs = a->num_seqs;
+  int grid = 0;
+  rc = c->dtype == B200_BF16
+           ? dispatch_d<BF16>(c->head_dim, mt, unused, unused, probe, info.num_sms, &grid, true, stream)
+           : dispatch_d<Half>(c->head_dim, mt, unused, unused, probe, info.num_sms, &grid, true, stream);
+  if (rc != B200_OK) return rc;
+  const WorkspaceLayout w = workspace_layout(a->num_seqs, c->num_kv_heads, group, c->head_dim, grid);
+  if (w.total > kDecodeNoAllocScratchBytes)
+    return set_error(B200_ERR_WORKSPACE,
+                     "this decode shape needs " + std::to_string(w.total) +
+                         " bytes of split scratch, more than the 8 MiB static scratch of "
+                         "b200_paged_decode_noalloc; use b200_paged_decode with a workspace");
+  void* scratch = nullptr;
+  rc = noalloc_scratch_address(&scratch);
+  if (rc != B200_OK) return rc;
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  cudaError_t err = cudaMemsetAsync(base + w.err_off, 0, 256, stream);
+  if (err != cudaSuccess) return cuda_status(err, "cudaMemsetAsync(scratch error word)");
+  err = cudaMemsetAsync(base + w.counters_off, 0, w.total - w.counters_off, stream);
+  if (err != cudaSuccess) return cuda_status(err, "cudaMemsetAsync(scratch counters)");
+  return launch_paged_decode(c, a, query, block_tables, context_lens, out, scratch,
+                             kDecodeNoAllocScratchBytes, stream);
 }
 
 }  // namespace b200

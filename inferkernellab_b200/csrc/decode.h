@@ -14,4 +14,10 @@ int launch_paged_decode(const b200_cache_desc* c, const b200_decode_args* a, con
                         const void* block_tables, const void* context_lens, void* out,
                         void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+// Allocation-free variant: split scratch from a static device array (decode.cu).
+size_t decode_noalloc_scratch_bytes();
+int launch_paged_decode_noalloc(const b200_cache_desc* c, const b200_decode_args* a,
+                                const void* query, const void* block_tables,
+                                const void* context_lens, void* out, cudaStream_t stream);
+
 }  // namespace b200
