@@ -120,7 +120,8 @@ class Workload:
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,"
+              "clocks.mem,clocks.max.mem")
 
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
@@ -150,7 +151,7 @@ class ClockSampler:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         rows = [r.split(",") for r in getattr(self, "out", "").strip().splitlines() if r.strip()]
-        sm, smax, reasons = [], None, set()
+        sm, smax, reasons, mem, mem_max = [], None, set(), [], None
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
             r = [x.strip() for x in r]
@@ -164,7 +165,14 @@ class ClockSampler:
             for name, flag in zip(names, r[5:9]):
                 if flag.lower() == "active":
                     reasons.add(name)
+            if len(r) >= 11:
+                try:
+                    mem.append(float(r[9]))
+                    mem_max = float(r[10])
+                except ValueError:
+                    pass
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "mem_mhz": statistics.median(mem) if mem else None, "mem_max_mhz": mem_max,
                 "reasons": sorted(reasons), "samples": len(sm),
                 "window": "nvidia-smi every 50 ms over warm-up + timed steps"}
 

@@ -3,8 +3,11 @@
 //   KvTileShape<D>   -- shared-memory geometry of one 64-token K/V tile as TMA
 //                       writes it: `chunks` column regions of 64 rows x
 //                       chunk_bytes, each 1024-byte aligned, optionally swizzled.
-//   issue_kv_tile()  -- producer side: block-table lookup, validity mask,
-//                       expect-tx and the TMA loads of one tile (one warp).
+//   TableWindow      -- producer-private shared-memory copy of part of a
+//                       block-table row (one coalesced refill per window).
+//   issue_kv_tile()  -- producer side: block ids, validity mask, expect-tx and
+//                       the TMA loads of one tile (one warp).
+//   block_exclusive_scan() -- warp-shuffle prefix sum over a CTA.
 //   load_q_frag()    -- 16 query rows x D as mma.sync A fragments.
 //   attend16()       -- consumer side: S = Q K^T for 16 keys, masking, base-2
 //                       online softmax and O += P V on mma.sync m16n8k16.
@@ -37,30 +40,75 @@ struct PagedSource {
   int box_rows;    // tokens per TMA box = min(block_size, 64)
 };
 
+// Producer-private window of one block-table row, kept in shared memory.  The
+// producer walks the pages of a request in order (and revisits them for the
+// next kv head), so one coalesced refill per window replaces a dependent
+// global load per tile on the TMA issue path.  Entries outside [0, num_blocks)
+// are stored as -1.
+constexpr int kTableWindow = 512;
+
+struct TableWindow {
+  int* ids;   // kTableWindow entries in shared memory
+  int row;    // table row held, -1 = none
+  int first;  // first page held
+  int count;  // pages held
+};
+
+__device__ __forceinline__ void table_window_refill(TableWindow& w, const PagedSource& src,
+                                                    int row, int first_page, int row_pages,
+                                                    uint32_t* err, int lane) {
+  const int count = min(kTableWindow, row_pages - first_page);
+  const long long base = static_cast<long long>(row) * src.table_stride + first_page;
+  __syncwarp();
+  for (int i0 = 0; i0 < count; i0 += 128) {
+    long long v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * 32 + lane;
+      v[u] = i < count ? load_index(src.tables, base + i, src.table64) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * 32 + lane;
+      if (i < count) {
+        const bool ok = v[u] >= 0 && v[u] < src.num_blocks;
+        if (!ok && err) atomicOr(err, kErrBadBlock);
+        w.ids[i] = ok ? static_cast<int>(v[u]) : -1;
+      }
+    }
+  }
+  __syncwarp();
+  w.row = row;
+  w.first = first_page;
+  w.count = count;
+}
+
 // Producer (whole warp): load logical tokens tok0 .. tok0+ntok-1 (ntok <= 64) of
 // table row `row` and kv head `head` into stage buffers kdst/vdst, arm `bar`,
 // and return the token-validity mask (bit i = tile row i holds a real token).
 // Pages whose block id is outside [0, num_blocks) are not loaded and masked.
+// `row_pages` = pages of the row that hold tokens (never read past them).
 template <int D>
 __device__ __forceinline__ void issue_kv_tile(const CUtensorMap* kmap, const CUtensorMap* vmap,
-                                              const PagedSource& src, int row, int head, int tok0,
-                                              int ntok, uint8_t* kdst, uint8_t* vdst,
-                                              uint64_t* bar, uint64_t* mask_out,
-                                              uint32_t* err, int lane) {
+                                              const PagedSource& src, TableWindow& win, int row,
+                                              int row_pages, int head, int tok0, int ntok,
+                                              uint8_t* kdst, uint8_t* vdst, uint64_t* bar,
+                                              uint64_t* mask_out, uint32_t* err, int lane) {
   using S = KvTileShape<D>;
   const int rows = src.box_rows;
   const int boxes = kKvTile / rows;
   const uint32_t box_bytes = static_cast<uint32_t>(rows) * S::kChunkBytes;
-  const long long row_base = static_cast<long long>(row) * src.table_stride;
+  const int first_page = tok0 / src.block_size;
+  const int last_page = (tok0 + ntok - 1) / src.block_size;
+  if (win.row != row || first_page < win.first || last_page >= win.first + win.count)
+    table_window_refill(win, src, row, first_page, row_pages, err, lane);
   uint32_t mlo = 0, mhi = 0, nvalid = 0;
   for (int j0 = 0; j0 < boxes; j0 += 32) {
     const int j = j0 + lane;
     bool ok = false;
     if (j < boxes && j * rows < ntok) {
       const int pos = tok0 + j * rows;
-      const long long blk = load_index(src.tables, row_base + pos / src.block_size, src.table64);
-      ok = blk >= 0 && blk < src.num_blocks;
-      if (!ok && err) atomicOr(err, kErrBadBlock);
+      ok = win.ids[pos / src.block_size - win.first] >= 0;
     }
     uint64_t m = 0;
     if (ok) {
@@ -82,9 +130,10 @@ __device__ __forceinline__ void issue_kv_tile(const CUtensorMap* kmap, const CUt
     const int j = j0 + lane;
     if (j < boxes && j * rows < ntok) {
       const int pos = tok0 + j * rows;
-      const long long blk = load_index(src.tables, row_base + pos / src.block_size, src.table64);
-      if (blk >= 0 && blk < src.num_blocks) {
-        const int z = static_cast<int>(src.layer_slot_base + blk * src.block_size +
+      const int blk = win.ids[pos / src.block_size - win.first];
+      if (blk >= 0) {
+        const int z = static_cast<int>(src.layer_slot_base +
+                                       static_cast<long long>(blk) * src.block_size +
                                        (pos & (src.block_size - 1)));
 #pragma unroll
         for (int c = 0; c < S::kChunks; ++c) {
@@ -95,6 +144,33 @@ __device__ __forceinline__ void issue_kv_tile(const CUtensorMap* kmap, const CUt
       }
     }
   }
+}
+
+// Exclusive prefix sum over the threads of a block of kThreads (a multiple of
+// 32): returns the sum of `v` over lower thread ids; *total gets the block sum.
+// `warp_tot` is shared scratch of kThreads / 32 ints.  Contains __syncthreads.
+template <int kThreads>
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot, int* total) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  int before = 0, all = 0;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w) {
+    const int t = warp_tot[w];
+    before += w < warp ? t : 0;
+    all += t;
+  }
+  __syncthreads();
+  *total = all;
+  return before + x - v;
 }
 
 // Bounded wait for the producer's last `kStages` armed phases before exit.
@@ -130,43 +206,80 @@ __device__ __forceinline__ void load_q_frag(uint32_t (&qf)[D / 16][4], const typ
   }
 }
 
-// One 16-key step of attention for a 16-row block held by one warp.
-//   kbase/vbase: shared addresses of the stage's K/V tile; `tok` = first tile
-//   row of the 16 keys; gmask = validity of those 16 keys (bit i = key tok+i).
-//   CAUSAL: additionally key (key_pos0 + i) must be < lim0 (row g) / lim1 (row g+8).
-template <typename E, int D, bool CAUSAL>
-__device__ __forceinline__ void attend16(const uint32_t (&qf)[D / 16][4], float (&o)[D / 8][4],
-                                         float (&m_r)[2], float (&l_r)[2], uint32_t kbase,
-                                         uint32_t vbase, int tok, uint32_t gmask, int key_pos0,
-                                         int lim0, int lim1, float scale_log2, uint32_t sw,
-                                         int lane) {
+// K and V fragments of 16 keys for mma.sync, held in registers so the stage
+// can be released before the math runs.
+template <int D>
+struct KvFrags {
+  uint32_t k[2][D / 16][2];  // per n-tile of 8 keys, per 16-dim k-step: b0, b1
+  uint32_t v[D / 8][2];      // per 8-dim n-tile of O: b0 (keys 0-7), b1 (keys 8-15)
+};
+
+// Load the fragments of the 16 keys starting at tile row `tok`.  V rows of
+// keys that are not real tokens (gmask bit clear) are zeroed so NaN/Inf in
+// unwritten slots cannot leak (0 * NaN = NaN); causally masked keys are real
+// tokens with finite values by contract and only need P = 0.
+template <int D>
+__device__ __forceinline__ void load_kv_frags(KvFrags<D>& f, uint32_t kbase, uint32_t vbase,
+                                              int tok, uint32_t gmask, uint32_t sw, int lane) {
   using S = KvTileShape<D>;
   const int tq = lane & 3;
-  float sacc[2][4];
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
-    sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
     const int trow = tok + nt * 8 + (lane & 7);
     if constexpr (D == 16) {
       const int d = ((lane >> 3) & 1) * 8;
-      const uint32_t addr = kbase + swizzle_offset(trow * S::kChunkBytes + d * 2, sw);
-      uint32_t b0, b1;
-      ldsm_x2(addr, b0, b1);
-      mma_16816<E>(sacc[nt], qf[0], b0, b1);
+      ldsm_x2(kbase + swizzle_offset(trow * S::kChunkBytes + d * 2, sw), f.k[nt][0][0],
+              f.k[nt][0][1]);
     } else {
 #pragma unroll
       for (int kk = 0; kk < D / 16; kk += 2) {
         const int d = kk * 16 + (lane >> 3) * 8;
         const int c = d / S::kChunkElems;
         const int dc = d - c * S::kChunkElems;
-        const uint32_t addr =
-            kbase + c * S::kRegionBytes + swizzle_offset(trow * S::kChunkBytes + dc * 2, sw);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(addr, b0, b1, b2, b3);
-        mma_16816<E>(sacc[nt], qf[kk], b0, b1);
-        mma_16816<E>(sacc[nt], qf[kk + 1], b2, b3);
+        ldsm_x4(kbase + c * S::kRegionBytes + swizzle_offset(trow * S::kChunkBytes + dc * 2, sw),
+                f.k[nt][kk][0], f.k[nt][kk][1], f.k[nt][kk + 1][0], f.k[nt][kk + 1][1]);
       }
     }
+  }
+  uint32_t keep0 = 0xffffffffu, keep1 = 0xffffffffu;
+  if (gmask != 0xffffu) {
+    keep0 = (((gmask >> (2 * tq)) & 1u) ? 0x0000ffffu : 0u) |
+            (((gmask >> (2 * tq + 1)) & 1u) ? 0xffff0000u : 0u);
+    keep1 = (((gmask >> (2 * tq + 8)) & 1u) ? 0x0000ffffu : 0u) |
+            (((gmask >> (2 * tq + 9)) & 1u) ? 0xffff0000u : 0u);
+  }
+  const int vrow = tok + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+  for (int dt = 0; dt < D / 8; dt += 2) {
+    const int d = dt * 8 + (lane >> 4) * 8;
+    const int c = d / S::kChunkElems;
+    const int dc = d - c * S::kChunkElems;
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4_t(vbase + c * S::kRegionBytes + swizzle_offset(vrow * S::kChunkBytes + dc * 2, sw),
+              b0, b1, b2, b3);
+    f.v[dt][0] = b0 & keep0;
+    f.v[dt][1] = b1 & keep1;
+    f.v[dt + 1][0] = b2 & keep0;
+    f.v[dt + 1][1] = b3 & keep1;
+  }
+}
+
+// One 16-key step of attention for a 16-row block held by one warp, from
+// fragments in registers.  gmask = validity of the 16 keys (bit i = key i);
+// CAUSAL: additionally key (key_pos0 + i) must be < lim0 (row g) / lim1 (row g+8).
+template <typename E, int D, bool CAUSAL>
+__device__ __forceinline__ void attend16_frags(const uint32_t (&qf)[D / 16][4],
+                                               float (&o)[D / 8][4], float (&m_r)[2],
+                                               float (&l_r)[2], const KvFrags<D>& f,
+                                               uint32_t gmask, int key_pos0, int lim0, int lim1,
+                                               float scale_log2, int lane) {
+  const int tq = lane & 3;
+  float sacc[2][4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) mma_16816<E>(sacc[nt], qf[kk], f.k[nt][kk][0], f.k[nt][kk][1]);
   }
   float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
@@ -215,9 +328,137 @@ __device__ __forceinline__ void attend16(const uint32_t (&qf)[D / 16][4], float 
   pa[1] = pack2<E>(sacc[0][2], sacc[0][3]);
   pa[2] = pack2<E>(sacc[1][0], sacc[1][1]);
   pa[3] = pack2<E>(sacc[1][2], sacc[1][3]);
-  // V rows of keys that are not real tokens are zeroed so NaN/Inf in unwritten
-  // slots cannot leak (0 * NaN = NaN).  Causally masked keys are real tokens
-  // with finite values by contract and only need P = 0.
+#pragma unroll
+  for (int dt = 0; dt < D / 8; ++dt) mma_16816<E>(o[dt], pa, f.v[dt][0], f.v[dt][1]);
+}
+
+// attend16 straight from shared memory (loads the fragments, then the math).
+template <typename E, int D, bool CAUSAL>
+__device__ __forceinline__ void attend16(const uint32_t (&qf)[D / 16][4], float (&o)[D / 8][4],
+                                         float (&m_r)[2], float (&l_r)[2], uint32_t kbase,
+                                         uint32_t vbase, int tok, uint32_t gmask, int key_pos0,
+                                         int lim0, int lim1, float scale_log2, uint32_t sw,
+                                         int lane) {
+  KvFrags<D> f;
+  load_kv_frags<D>(f, kbase, vbase, tok, gmask, sw, lane);
+  attend16_frags<E, D, CAUSAL>(qf, o, m_r, l_r, f, gmask, key_pos0, lim0, lim1, scale_log2, lane);
+}
+
+// ------------------------------------------------------------------------
+// Transposed decode step (query group as the MMA N dimension).
+//
+// For decode, the G query heads that share a KV head are few (G <= 16 here),
+// so they become the N = 8 * NT columns of mma.m16n8k16 and the 16 keys of a
+// step become the M rows:  S^T[16 keys x 8NT heads] = K[16 x D] . Q^T[D x 8NT],
+// O^T[D x 8NT] += V^T[D x 16] . P^T[16 x 8NT].  At G = 4 this needs half the
+// MMAs and half the O registers of the heads-as-M form (N pads 4 -> 8, M would
+// pad 4 -> 16).  P^T leaves the first MMA in accumulator layout; movmatrix
+// transposes its 8x8 halves into the B-operand layout of the second.
+
+// Q^T as B fragments: b0 = Q[head n*8+g][16k + 2t, +1], b1 = ... + 8.
+template <typename E, int D, int NT>
+__device__ __forceinline__ void load_qT_frag(uint32_t (&qb)[NT][D / 16][2],
+                                             const typename E::T* q_group, long long head_stride,
+                                             int group, int lane) {
+  const int g = lane >> 2;
+  const int tq = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int head = nt * 8 + g;
+    const typename E::T* row = q_group + head * head_stride;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      qb[nt][kk][0] = head < group ? *reinterpret_cast<const uint32_t*>(row + kk * 16 + 2 * tq) : 0u;
+      qb[nt][kk][1] =
+          head < group ? *reinterpret_cast<const uint32_t*>(row + kk * 16 + 8 + 2 * tq) : 0u;
+    }
+  }
+}
+
+// One 16-key step.  State per thread: m/l for heads (n*8 + 2t, +1) (m is
+// uniform over the 8 lanes g; l is this thread's partial over its keys g, g+8),
+// oT[n][i] = O^T rows (dims) 16i+g, 16i+g+8 x heads n*8+2t, +1.
+template <typename E, int D, int NT>
+__device__ __forceinline__ void decode_step16_T(const uint32_t (&qb)[NT][D / 16][2],
+                                                float (&oT)[NT][D / 16][4], float (&m)[NT][2],
+                                                float (&l)[NT][2], uint32_t kbase, uint32_t vbase,
+                                                int tok, uint32_t gmask, float scale_log2,
+                                                uint32_t sw, int lane) {
+  using S = KvTileShape<D>;
+  const int g = lane >> 2;
+  const int tq = lane & 3;
+  const int mi = lane >> 3;
+  // ---- S^T = K Q^T, two independent accumulation chains over the k-steps ----
+  float sa[NT][4], sb[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sa[nt][e] = sb[nt][e] = 0.f;
+  const int krow = tok + (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int d = kk * 16 + (mi >> 1) * 8;
+    const int c = d / S::kChunkElems;
+    const int dc = d - c * S::kChunkElems;
+    uint32_t a[4];
+    ldsm_x4(kbase + c * S::kRegionBytes + swizzle_offset(krow * S::kChunkBytes + dc * 2, sw), a[0],
+            a[1], a[2], a[3]);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      if (kk & 1)
+        mma_16816<E>(sb[nt], a, qb[nt][kk][0], qb[nt][kk][1]);
+      else
+        mma_16816<E>(sa[nt], a, qb[nt][kk][0], qb[nt][kk][1]);
+    }
+  }
+  // ---- mask (keys g, g+8 of this step), scale, online softmax per head ----
+  const bool v_lo = (gmask >> g) & 1u;
+  const bool v_hi = (gmask >> (g + 8)) & 1u;
+  float p[NT][4];
+  float alpha[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float s0 = v_lo ? (sa[nt][0] + sb[nt][0]) * scale_log2 : -INFINITY;
+    float s1 = v_lo ? (sa[nt][1] + sb[nt][1]) * scale_log2 : -INFINITY;
+    float s2 = v_hi ? (sa[nt][2] + sb[nt][2]) * scale_log2 : -INFINITY;
+    float s3 = v_hi ? (sa[nt][3] + sb[nt][3]) * scale_log2 : -INFINITY;
+    float mx0 = fmaxf(s0, s2);  // head 2t
+    float mx1 = fmaxf(s1, s3);  // head 2t+1
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    const float mn0 = fmaxf(m[nt][0], mx0);
+    const float mn1 = fmaxf(m[nt][1], mx1);
+    const float base0 = mn0 == -INFINITY ? 0.f : mn0;
+    const float base1 = mn1 == -INFINITY ? 0.f : mn1;
+    alpha[nt][0] = fast_exp2(m[nt][0] - base0);
+    alpha[nt][1] = fast_exp2(m[nt][1] - base1);
+    m[nt][0] = mn0;
+    m[nt][1] = mn1;
+    p[nt][0] = fast_exp2(s0 - base0);
+    p[nt][1] = fast_exp2(s1 - base1);
+    p[nt][2] = fast_exp2(s2 - base0);
+    p[nt][3] = fast_exp2(s3 - base1);
+    l[nt][0] = l[nt][0] * alpha[nt][0] + (p[nt][0] + p[nt][2]);
+    l[nt][1] = l[nt][1] * alpha[nt][1] + (p[nt][1] + p[nt][3]);
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) {
+      oT[nt][i][0] *= alpha[nt][0];
+      oT[nt][i][1] *= alpha[nt][1];
+      oT[nt][i][2] *= alpha[nt][0];
+      oT[nt][i][3] *= alpha[nt][1];
+    }
+  }
+  // ---- P^T into B-operand layout (transpose each 8x8 half) ----
+  uint32_t pb[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    pb[nt][0] = movmatrix_trans(pack2<E>(p[nt][0], p[nt][1]));  // keys 0-7
+    pb[nt][1] = movmatrix_trans(pack2<E>(p[nt][2], p[nt][3]));  // keys 8-15
+  }
+  // V rows of keys that are not real tokens are zeroed: 0 * NaN would leak.
   uint32_t keep0 = 0xffffffffu, keep1 = 0xffffffffu;
   if (gmask != 0xffffu) {
     keep0 = (((gmask >> (2 * tq)) & 1u) ? 0x0000ffffu : 0u) |
@@ -225,22 +466,22 @@ __device__ __forceinline__ void attend16(const uint32_t (&qf)[D / 16][4], float 
     keep1 = (((gmask >> (2 * tq + 8)) & 1u) ? 0x0000ffffu : 0u) |
             (((gmask >> (2 * tq + 9)) & 1u) ? 0xffff0000u : 0u);
   }
-  const int vrow = tok + ((lane >> 3) & 1) * 8 + (lane & 7);
+  // ---- O^T += V^T P^T ----
+  const int vrow = tok + (mi >> 1) * 8 + (lane & 7);
 #pragma unroll
-  for (int dt = 0; dt < D / 8; dt += 2) {
-    const int d = dt * 8 + (lane >> 4) * 8;
+  for (int i = 0; i < D / 16; ++i) {
+    const int d = i * 16 + (mi & 1) * 8;
     const int c = d / S::kChunkElems;
     const int dc = d - c * S::kChunkElems;
-    const uint32_t addr =
-        vbase + c * S::kRegionBytes + swizzle_offset(vrow * S::kChunkBytes + dc * 2, sw);
-    uint32_t b0, b1, b2, b3;
-    ldsm_x4_t(addr, b0, b1, b2, b3);
-    b0 &= keep0;
-    b2 &= keep0;
-    b1 &= keep1;
-    b3 &= keep1;
-    mma_16816<E>(o[dt], pa, b0, b1);
-    mma_16816<E>(o[dt + 1], pa, b2, b3);
+    uint32_t a[4];
+    ldsm_x4_t(vbase + c * S::kRegionBytes + swizzle_offset(vrow * S::kChunkBytes + dc * 2, sw),
+              a[0], a[1], a[2], a[3]);
+    a[0] &= keep0;
+    a[1] &= keep0;
+    a[2] &= keep1;
+    a[3] &= keep1;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) mma_16816<E>(oT[nt][i], a, pb[nt][0], pb[nt][1]);
   }
 }
 

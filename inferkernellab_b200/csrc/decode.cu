@@ -63,6 +63,8 @@ struct DecodeParams {
   float scale_log2;
 };
 
+// Ring depth per CTA and CTAs per SM (kDecMinBlocks feeds __launch_bounds__).
+constexpr int kDecMinBlocks = 2;
 template <int D>
 struct DecodeShape : KvTileShape<D> {
   static constexpr int kStages = D >= 128 ? 3 : 4;
@@ -70,19 +72,23 @@ struct DecodeShape : KvTileShape<D> {
 
 // Shared-memory carve-up (offsets from a 1024-byte aligned base).
 struct DecodeSmem {
-  int stage_bytes;     // K + V of one stage
-  int bars_off;        // full[S], empty[S]
-  int mask_off;        // uint64 per stage
-  int flags_off;       // abort, merge flag
-  int red_m_off, red_l_off, red_o_off;
+  int stage_bytes;  // K + V of one stage
+  int bars_off;     // full[S], empty[S]
+  int mask_off;     // uint64 per stage
+  int flags_off;    // abort, merge flag
+  int red_m_off, red_l_off, red_w_off, row_off, red_o_off, merge_w_off;
+  int table_off;    // producer's block-table window
   int len_off, begin_off, scan_off;
   int total;
 };
 
+constexpr int kMergeChunk = 32;  // split pieces merged per pass
+
 template <int D, int MT>
 __host__ __device__ inline DecodeSmem decode_smem_layout(int group, int num_seqs) {
   using S = DecodeShape<D>;
-  constexpr int kSlices = kDecConsumerWarps / MT;
+  constexpr int kSlices = MT < 0 ? kDecConsumerWarps : kDecConsumerWarps / MT;
+  constexpr int kRows = MT < 0 ? 8 * -MT : 16 * MT;
   DecodeSmem L;
   L.stage_bytes = 2 * S::kTileBytes;
   int off = S::kStages * L.stage_bytes;
@@ -93,18 +99,26 @@ __host__ __device__ inline DecodeSmem decode_smem_layout(int group, int num_seqs
   L.flags_off = off;
   off += 16;
   L.red_m_off = off;
-  off += kSlices * 16 * MT * 4;
+  off += kSlices * kRows * 4;
   L.red_l_off = off;
-  off += kSlices * 16 * MT * 4;
+  off += kSlices * kRows * 4;
+  L.red_w_off = off;
+  off += kSlices * kRows * 4;
+  L.row_off = off;  // base and 1/l (or sum) per row
+  off += 2 * kRows * 4;
   off = (off + 15) & ~15;
   L.red_o_off = off;
   off += kSlices * group * D * 4;
+  L.merge_w_off = off;
+  off += kMergeChunk * group * 4;
+  L.table_off = off;
+  off += kTableWindow * 4;
   L.len_off = off;
   off += num_seqs * 4;
   L.begin_off = off;
   off += (num_seqs + 1) * 4;
   L.scan_off = off;
-  off += kDecThreads * 4;
+  off += (kDecThreads / 32) * 4;
   L.total = off;
   return L;
 }
@@ -143,16 +157,47 @@ __device__ __forceinline__ float fast_log2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Store four consecutive output elements (8 bytes).
+template <typename E>
+__device__ __forceinline__ void store4(typename E::T* dst, float4 v) {
+  uint2 packed;
+  packed.x = pack2<E>(v.x, v.y);
+  packed.y = pack2<E>(v.z, v.w);
+  *reinterpret_cast<uint2*>(dst) = packed;
+}
+
+constexpr int kMinTilesPerCta = 2;  // fewer split pieces on small problems
+
 template <typename E, int D, int MT>
-__global__ void __launch_bounds__(kDecThreads, 2)
+__global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
   using S = DecodeShape<D>;
   using T = typename E::T;
-  constexpr int kSlices = kDecConsumerWarps / MT;
+  // MT > 0: query heads are the MMA M rows (MT m-tiles of 16, for G > 16).
+  // MT < 0: transposed form, keys are M and the group is N = 8 * (-MT) (G <= 16).
+  constexpr bool kTrans = MT < 0;
+  constexpr int NT = kTrans ? -MT : 1;
+  constexpr int kSlices = kTrans ? kDecConsumerWarps : kDecConsumerWarps / MT;
+  constexpr int kRows = kTrans ? 8 * NT : 16 * MT;
   constexpr int kTokPerWarp = kDecTile / kSlices;  // 16, 32 or 64
   constexpr int kGroups16 = kTokPerWarp / 16;
   constexpr int kStages = S::kStages;
+  constexpr int kConsumers = kDecConsumerWarps * 32;
+  constexpr int kD4 = D / 4;
+  constexpr int kElems4 = (kRows * kD4 + kConsumers - 1) / kConsumers;  // float4 per thread
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -165,7 +210,11 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   int* merge_flag = reinterpret_cast<int*>(smem + L.flags_off + 4);
   float* red_m = reinterpret_cast<float*>(smem + L.red_m_off);
   float* red_l = reinterpret_cast<float*>(smem + L.red_l_off);
+  float* red_w = reinterpret_cast<float*>(smem + L.red_w_off);
+  float* row_base = reinterpret_cast<float*>(smem + L.row_off);
+  float* row_l = row_base + kRows;
   float* red_o = reinterpret_cast<float*>(smem + L.red_o_off);
+  float* merge_w = reinterpret_cast<float*>(smem + L.merge_w_off);
   int* len_s = reinterpret_cast<int*>(smem + L.len_off);
   int* begin_s = reinterpret_cast<int*>(smem + L.begin_off);
   int* scan_s = reinterpret_cast<int*>(smem + L.scan_off);
@@ -199,27 +248,17 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   __syncthreads();
   {
     const int chunk = (B + kDecThreads - 1) / kDecThreads;
-    const int lo = tid * chunk;
+    const int lo = min(B, tid * chunk);
     const int hi = min(B, lo + chunk);
     int sum = 0;
     for (int i = lo; i < hi; ++i) sum += ((len_s[i] + kDecTile - 1) / kDecTile) * HKV;
-    scan_s[tid] = sum;
-    __syncthreads();
-    if (tid == 0) {
-      int acc = 0;
-      for (int i = 0; i < kDecThreads; ++i) {
-        int v = scan_s[i];
-        scan_s[i] = acc;
-        acc += v;
-      }
-      begin_s[B] = acc;
-    }
-    __syncthreads();
-    int acc = scan_s[tid];
+    int total_all = 0;
+    int acc = block_exclusive_scan<kDecThreads>(sum, scan_s, &total_all);
     for (int i = lo; i < hi; ++i) {
       begin_s[i] = acc;
       acc += ((len_s[i] + kDecTile - 1) / kDecTile) * HKV;
     }
+    if (tid == 0) begin_s[B] = total_all;
   }
   __syncthreads();
 
@@ -228,7 +267,7 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     for (int r = 0; r < B; ++r) {
       if (len_s[r] != 0) continue;
       const int nh = HKV * G;
-      for (int i = tid; i < nh * D; i += kDecConsumerWarps * 32) {
+      for (int i = tid; i < nh * D; i += kConsumers) {
         const int hq = i / D, d = i - hq * D;
         reinterpret_cast<T*>(p.out)[r * p.out_stride_seq + hq * p.out_stride_head + d] =
             from_float<E>(__int_as_float(0x7fc00000));
@@ -236,8 +275,12 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     }
   }
 
+  // ---- this CTA's contiguous range of tiles (stream-K) ----
   const int total = begin_s[B];
-  const int per_cta = (total + gridDim.x - 1) / gridDim.x;
+  const int ctas = min(static_cast<int>(gridDim.x),
+                       max(1, (total + kMinTilesPerCta - 1) / kMinTilesPerCta));
+  if (static_cast<int>(blockIdx.x) >= ctas) return;
+  const int per_cta = (total + ctas - 1) / ctas;
   const int my_begin = min(total, static_cast<int>(blockIdx.x) * per_cta);
   const int my_end = min(total, my_begin + per_cta);
   const int n_tiles = my_end - my_begin;
@@ -255,6 +298,11 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     src.num_blocks = p.num_blocks;
     src.block_size = p.block_size;
     src.box_rows = p.box_rows;
+    TableWindow win;
+    win.ids = reinterpret_cast<int*>(smem + L.table_off);
+    win.row = -1;
+    win.first = 0;
+    win.count = 0;
     TileCursor cur;
     cur.init(my_begin, begin_s, len_s, B, HKV);
     int issued = 0;
@@ -263,11 +311,13 @@ __global__ void __launch_bounds__(kDecThreads, 2)
       const uint32_t k = static_cast<uint32_t>(it / kStages);
       if (!mbar_wait_bounded(&empty_bar[s], (k & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty))
         break;
+      const int len = len_s[cur.r];
       const int tok0 = cur.t * kDecTile;
-      const int ntok = min(kDecTile, len_s[cur.r] - tok0);
+      const int ntok = min(kDecTile, len - tok0);
       uint8_t* kdst = smem + s * L.stage_bytes;
-      issue_kv_tile<D>(&kmap, &vmap, src, cur.r, cur.h, tok0, ntok, kdst, kdst + S::kTileBytes,
-                       &full_bar[s], &stage_mask[s], p.err, lane);
+      issue_kv_tile<D>(&kmap, &vmap, src, win, cur.r, (len + p.block_size - 1) / p.block_size,
+                       cur.h, tok0, ntok, kdst, kdst + S::kTileBytes, &full_bar[s],
+                       &stage_mask[s], p.err, lane);
       ++issued;
       cur.advance(len_s, B, HKV);
     }
@@ -278,17 +328,22 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   }
 
   // ================================ consumers ================================
-  const int mt = warp % MT;
-  const int slice = warp / MT;
+  const int mt = kTrans ? 0 : warp % (kTrans ? 1 : MT);
+  const int slice = kTrans ? warp : warp / (kTrans ? 1 : MT);
   const int g = lane >> 2;
   const int tq = lane & 3;
-  const int row0 = mt * 16 + g;  // query-head row inside the group
+  const int row0 = mt * 16 + g;  // heads-as-M: query-head row inside the group
   const int row1 = row0 + 8;
   const uint32_t sw = static_cast<uint32_t>(p.sw_mask);
 
+  // heads-as-M state
   uint32_t qf[D / 16][4];
   float o[D / 8][4];
   float m_r[2], l_r[2];
+  // transposed state
+  uint32_t qb[NT][D / 16][2];
+  float oT[NT][D / 16][4];
+  float m_t[NT][2], l_t[NT][2];
   bool aborted = false;
 
   TileCursor cur;
@@ -298,14 +353,25 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   for (int it = 0; it < n_tiles; ++it) {
     if (seg_start) {
       seg_start = false;
-      const T* qb = reinterpret_cast<const T*>(p.q) + cur.r * p.q_stride_seq +
+      const T* qg = reinterpret_cast<const T*>(p.q) + cur.r * p.q_stride_seq +
                     static_cast<long long>(cur.h * G) * p.q_stride_head;
-      load_q_frag<E, D>(qf, row0 < G ? qb + row0 * p.q_stride_head : nullptr,
-                        row1 < G ? qb + row1 * p.q_stride_head : nullptr, tq);
+      if constexpr (kTrans) {
+        load_qT_frag<E, D, NT>(qb, qg, p.q_stride_head, G, lane);
 #pragma unroll
-      for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-      m_r[0] = m_r[1] = -INFINITY;
-      l_r[0] = l_r[1] = 0.f;
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+          for (int i = 0; i < D / 16; ++i) oT[nt][i][0] = oT[nt][i][1] = oT[nt][i][2] = oT[nt][i][3] = 0.f;
+          m_t[nt][0] = m_t[nt][1] = -INFINITY;
+          l_t[nt][0] = l_t[nt][1] = 0.f;
+        }
+      } else {
+        load_q_frag<E, D>(qf, row0 < G ? qg + row0 * p.q_stride_head : nullptr,
+                          row1 < G ? qg + row1 * p.q_stride_head : nullptr, tq);
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+        m_r[0] = m_r[1] = -INFINITY;
+        l_r[0] = l_r[1] = 0.f;
+      }
     }
 
     const int s = it % kStages;
@@ -319,11 +385,15 @@ __global__ void __launch_bounds__(kDecThreads, 2)
       const uint32_t vbase = kbase + S::kTileBytes;
 #pragma unroll
       for (int gi = 0; gi < kGroups16; ++gi) {
-        const int tok = slice * kTokPerWarp + gi * 16;  // first tile row of this 16-token group
+        const int tok = slice * kTokPerWarp + gi * 16;  // first tile row of this 16-key group
         const uint32_t gmask = static_cast<uint32_t>(tmask >> tok) & 0xffffu;
         if (gmask == 0) continue;
-        attend16<E, D, false>(qf, o, m_r, l_r, kbase, vbase, tok, gmask, 0, 0, 0, p.scale_log2,
-                              sw, lane);
+        if constexpr (kTrans)
+          decode_step16_T<E, D, NT>(qb, oT, m_t, l_t, kbase, vbase, tok, gmask, p.scale_log2, sw,
+                                    lane);
+        else
+          attend16<E, D, false>(qf, o, m_r, l_r, kbase, vbase, tok, gmask, 0, 0, 0,
+                                p.scale_log2, sw, lane);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[s]);
@@ -336,100 +406,207 @@ __global__ void __launch_bounds__(kDecThreads, 2)
       const int seg_begin = begin_s[cur.r] + cur.h * cur.nt;
       const int seg_end_tile = seg_begin + cur.nt;
       const bool complete = seg_begin >= my_begin && seg_end_tile <= my_end;
-      const float l0 = quad_sum(l_r[0]);
-      const float l1 = quad_sum(l_r[1]);
-      if (!aborted) {
-        if (tq == 0) {
-          red_m[slice * 16 * MT + row0] = m_r[0];
-          red_m[slice * 16 * MT + row1] = m_r[1];
-          red_l[slice * 16 * MT + row0] = l0;
-          red_l[slice * 16 * MT + row1] = l1;
-        }
-        if (row0 < G) {
-          float* dst = red_o + (slice * G + row0) * D + 2 * tq;
+      const int slot = seg_begin <= my_begin ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
+      T* out_seg = reinterpret_cast<T*>(p.out) + cur.r * p.out_stride_seq +
+                   static_cast<long long>(cur.h * G) * p.out_stride_head;
+      if constexpr (kTrans) {
+        // l: reduce each head's partial over the 8 key lanes (g).
 #pragma unroll
-          for (int i = 0; i < D / 8; ++i)
-            *reinterpret_cast<float2*>(dst + i * 8) = make_float2(o[i][0], o[i][1]);
-        }
-        if (row1 < G) {
-          float* dst = red_o + (slice * G + row1) * D + 2 * tq;
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int i = 0; i < D / 8; ++i)
-            *reinterpret_cast<float2*>(dst + i * 8) = make_float2(o[i][2], o[i][3]);
+          for (int j = 0; j < 2; ++j) {
+            float v = l_t[nt][j];
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            l_t[nt][j] = v;
+          }
+        if (!aborted) {
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const int h0 = nt * 8 + 2 * tq;
+            if (g == 0) {
+              red_m[slice * kRows + h0] = m_t[nt][0];
+              red_m[slice * kRows + h0 + 1] = m_t[nt][1];
+              red_l[slice * kRows + h0] = l_t[nt][0];
+              red_l[slice * kRows + h0 + 1] = l_t[nt][1];
+            }
+#pragma unroll
+            for (int i = 0; i < D / 16; ++i) {
+              const int d0 = i * 16 + g;
+              if (h0 < G) {
+                float* dst = red_o + (slice * G + h0) * D;
+                dst[d0] = oT[nt][i][0];
+                dst[d0 + 8] = oT[nt][i][2];
+              }
+              if (h0 + 1 < G) {
+                float* dst = red_o + (slice * G + h0 + 1) * D;
+                dst[d0] = oT[nt][i][1];
+                dst[d0 + 8] = oT[nt][i][3];
+              }
+            }
+          }
+        }
+      } else {
+        const float l0 = quad_sum(l_r[0]);
+        const float l1 = quad_sum(l_r[1]);
+        if (!aborted) {
+          if (tq == 0) {
+            red_m[slice * kRows + row0] = m_r[0];
+            red_m[slice * kRows + row1] = m_r[1];
+            red_l[slice * kRows + row0] = l0;
+            red_l[slice * kRows + row1] = l1;
+          }
+          if (row0 < G) {
+            float* dst = red_o + (slice * G + row0) * D + 2 * tq;
+#pragma unroll
+            for (int i = 0; i < D / 8; ++i)
+              *reinterpret_cast<float2*>(dst + i * 8) = make_float2(o[i][0], o[i][1]);
+          }
+          if (row1 < G) {
+            float* dst = red_o + (slice * G + row1) * D + 2 * tq;
+#pragma unroll
+            for (int i = 0; i < D / 8; ++i)
+              *reinterpret_cast<float2*>(dst + i * 8) = make_float2(o[i][2], o[i][3]);
+          }
         }
       }
-      named_bar_sync(1, kDecConsumerWarps * 32);
-      const int slot = seg_begin <= my_begin ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
+      named_bar_sync(1, kConsumers);
+      // Per-row slice weights, once per row.
       if (!aborted) {
-        for (int idx = tid; idx < G * D; idx += kDecConsumerWarps * 32) {
-          const int row = idx / D;
-          const int d = idx - row * D;
-          const int mrow = (row >> 4) * 16 + (row & 15);  // row inside its m-tile block
+        for (int row = tid; row < G; row += kConsumers) {
           float mmax = -INFINITY;
 #pragma unroll
-          for (int sl = 0; sl < kSlices; ++sl) mmax = fmaxf(mmax, red_m[sl * 16 * MT + mrow]);
+          for (int sl = 0; sl < kSlices; ++sl) mmax = fmaxf(mmax, red_m[sl * kRows + row]);
           const float base = mmax == -INFINITY ? 0.f : mmax;
-          float lsum = 0.f, osum = 0.f;
+          float lsum = 0.f;
 #pragma unroll
           for (int sl = 0; sl < kSlices; ++sl) {
-            const float w = fast_exp2(red_m[sl * 16 * MT + mrow] - base);
-            lsum += red_l[sl * 16 * MT + mrow] * w;
-            osum += red_o[(sl * G + row) * D + d] * w;
+            const float w = fast_exp2(red_m[sl * kRows + row] - base);
+            red_w[sl * kRows + row] = w;
+            lsum += red_l[sl * kRows + row] * w;
           }
-          if (complete) {
-            reinterpret_cast<T*>(p.out)[cur.r * p.out_stride_seq +
-                                        (cur.h * G + row) * p.out_stride_head + d] =
-                from_float<E>(osum / lsum);
-          } else {
-            p.part_o[(static_cast<long long>(slot) * G + row) * D + d] = osum / lsum;
-            if (d == 0) p.part_lse[slot * G + row] = lsum > 0.f ? base + fast_log2(lsum) : -INFINITY;
+          row_base[row] = base;
+          row_l[row] = lsum;
+          if (!complete)
+            p.part_lse[slot * G + row] = lsum > 0.f ? base + fast_log2(lsum) : -INFINITY;
+        }
+      }
+      named_bar_sync(1, kConsumers);
+      if (!aborted) {
+        for (int e = tid; e < G * kD4; e += kConsumers) {
+          const int row = e / kD4;
+          const int d4 = e - row * kD4;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int sl = 0; sl < kSlices; ++sl) {
+            const float w = red_w[sl * kRows + row];
+            const float4 v = reinterpret_cast<const float4*>(red_o + (sl * G + row) * D)[d4];
+            acc.x += w * v.x;
+            acc.y += w * v.y;
+            acc.z += w * v.z;
+            acc.w += w * v.w;
           }
+          const float inv = 1.f / row_l[row];
+          acc.x *= inv;
+          acc.y *= inv;
+          acc.z *= inv;
+          acc.w *= inv;
+          if (complete)
+            store4<E>(out_seg + row * p.out_stride_head + d4 * 4, acc);
+          else
+            reinterpret_cast<float4*>(p.part_o)[(static_cast<long long>(slot) * G + row) * kD4 +
+                                                d4] = acc;
         }
       }
       if (!complete) {
         __threadfence();
-        named_bar_sync(1, kDecConsumerWarps * 32);
+        named_bar_sync(1, kConsumers);
+        const int p_first = seg_begin / per_cta;
+        const int npieces = (seg_end_tile - 1) / per_cta - p_first + 1;
         if (tid == 0) {
           int last = 0;
-          if (!aborted) {
-            const int p_first = seg_begin / per_cta;
-            const int p_last = (seg_end_tile - 1) / per_cta;
-            const int prev = atomicAdd(&p.counters[seg], 1);
-            last = prev == p_last - p_first;
-          }
+          if (!aborted) last = atomicAdd(&p.counters[seg], 1) == npieces - 1;
           *merge_flag = last;
         }
-        named_bar_sync(1, kDecConsumerWarps * 32);
+        named_bar_sync(1, kConsumers);
         if (*merge_flag) {
+          // Last piece in: merge all pieces of the segment.  Piece i was written
+          // by CTA q = p_first + i into slot 2q (segment began at or before q's
+          // range) or 2q+1 (it began inside q's range).
           __threadfence();
-          const int p_first = seg_begin / per_cta;
-          const int p_last = (seg_end_tile - 1) / per_cta;
-          for (int idx = tid; idx < G * D; idx += kDecConsumerWarps * 32) {
-            const int row = idx / D;
-            const int d = idx - row * D;
+          auto piece_slot = [&](int i) {
+            const int q = p_first + i;
+            return seg_begin <= q * per_cta ? 2 * q : 2 * q + 1;
+          };
+          for (int row = warp; row < G; row += kDecConsumerWarps) {
             float mmax = -INFINITY;
-            for (int q = p_first; q <= p_last; ++q) {
-              const int sl = seg_begin <= q * per_cta ? 2 * q : 2 * q + 1;
-              mmax = fmaxf(mmax, __ldcg(p.part_lse + sl * G + row));
-            }
+            for (int i = lane; i < npieces; i += 32)
+              mmax = fmaxf(mmax, __ldcg(p.part_lse + piece_slot(i) * G + row));
+            mmax = warp_max(mmax);
             const float base = mmax == -INFINITY ? 0.f : mmax;
-            float wsum = 0.f, osum = 0.f;
-            for (int q = p_first; q <= p_last; ++q) {
-              const int sl = seg_begin <= q * per_cta ? 2 * q : 2 * q + 1;
-              const float lse = __ldcg(p.part_lse + sl * G + row);
-              if (lse == -INFINITY) continue;  // piece saw only masked tokens
-              const float w = fast_exp2(lse - base);
-              wsum += w;
-              osum += w * __ldcg(p.part_o + (static_cast<long long>(sl) * G + row) * D + d);
+            float wsum = 0.f;
+            for (int i = lane; i < npieces; i += 32) {
+              const float lse = __ldcg(p.part_lse + piece_slot(i) * G + row);
+              if (lse != -INFINITY) wsum += fast_exp2(lse - base);
             }
-            reinterpret_cast<T*>(p.out)[cur.r * p.out_stride_seq +
-                                        (cur.h * G + row) * p.out_stride_head + d] =
-                from_float<E>(osum / wsum);
+            wsum = warp_sum(wsum);
+            if (lane == 0) {
+              row_base[row] = base;
+              row_l[row] = 1.f / wsum;
+            }
+          }
+          named_bar_sync(1, kConsumers);
+          float4 acc[kElems4];
+#pragma unroll
+          for (int k4 = 0; k4 < kElems4; ++k4) acc[k4] = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int c0 = 0; c0 < npieces; c0 += kMergeChunk) {
+            const int nq = min(kMergeChunk, npieces - c0);
+            for (int i = tid; i < kMergeChunk * G; i += kConsumers) {
+              const int q = i / G;
+              const int row = i - q * G;
+              float w = 0.f;
+              if (q < nq) {
+                const float lse = __ldcg(p.part_lse + piece_slot(c0 + q) * G + row);
+                if (lse != -INFINITY) w = fast_exp2(lse - row_base[row]) * row_l[row];
+              }
+              merge_w[i] = w;
+            }
+            named_bar_sync(1, kConsumers);
+#pragma unroll
+            for (int k4 = 0; k4 < kElems4; ++k4) {
+              const int e = tid + k4 * kConsumers;
+              if (e < G * kD4) {
+                const int row = e / kD4;
+                const int d4 = e - row * kD4;
+#pragma unroll 4
+                for (int q = 0; q < nq; ++q) {
+                  const float w = merge_w[q * G + row];
+                  if (w == 0.f) continue;
+                  const float4 v = __ldcg(reinterpret_cast<const float4*>(p.part_o) +
+                                          (static_cast<long long>(piece_slot(c0 + q)) * G + row) *
+                                              kD4 + d4);
+                  acc[k4].x += w * v.x;
+                  acc[k4].y += w * v.y;
+                  acc[k4].z += w * v.z;
+                  acc[k4].w += w * v.w;
+                }
+              }
+            }
+            named_bar_sync(1, kConsumers);
+          }
+#pragma unroll
+          for (int k4 = 0; k4 < kElems4; ++k4) {
+            const int e = tid + k4 * kConsumers;
+            if (e < G * kD4) {
+              const int row = e / kD4;
+              store4<E>(out_seg + row * p.out_stride_head + (e - row * kD4) * 4, acc[k4]);
+            }
           }
           if (tid == 0) p.counters[seg] = 0;
         }
       }
-      named_bar_sync(1, kDecConsumerWarps * 32);
+      named_bar_sync(1, kConsumers);
       seg_start = true;
     }
     cur.advance(len_s, B, HKV);
@@ -496,11 +673,18 @@ static int launch_decode_t(const CUtensorMap& kmap, const CUtensorMap& vmap,
   return cuda_status(cudaGetLastError(), "paged_decode_kernel launch");
 }
 
+// Variant code per head group G: -1 (G <= 8) and -2 (G <= 16) use the
+// transposed form; 2 (G <= 32) and 4 (G <= 64) put the heads on the M rows.
+static int decode_variant(int group) {
+  return group <= 8 ? -1 : (group <= 16 ? -2 : (group <= 32 ? 2 : 4));
+}
+
 template <typename E, int D>
 static int dispatch_mt(int mt, const CUtensorMap& kmap, const CUtensorMap& vmap,
                        const DecodeParams& p, int num_sms, int* grid, bool dry, cudaStream_t s) {
   switch (mt) {
-    case 1: return launch_decode_t<E, D, 1>(kmap, vmap, p, num_sms, grid, dry, s);
+    case -1: return launch_decode_t<E, D, -1>(kmap, vmap, p, num_sms, grid, dry, s);
+    case -2: return launch_decode_t<E, D, -2>(kmap, vmap, p, num_sms, grid, dry, s);
     case 2: return launch_decode_t<E, D, 2>(kmap, vmap, p, num_sms, grid, dry, s);
     default: return launch_decode_t<E, D, 4>(kmap, vmap, p, num_sms, grid, dry, s);
   }
@@ -544,8 +728,10 @@ static int check_decode_args(const b200_cache_desc* c, const b200_decode_args* a
   if (slots >= (1ll << 31)) return set_error(B200_ERR_UNSUPPORTED, "cache has more than 2^31 slots");
   if (static_cast<int64_t>(a->table_width) * c->block_size >= (1ll << 30))
     return set_error(B200_ERR_UNSUPPORTED, "block table capacity too large");
-  if ((a->q_stride_seq | a->q_stride_head | a->out_stride_seq | a->out_stride_head) & 1)
-    return set_error(B200_ERR_INVALID, "query/out strides must be even");
+  if ((a->q_stride_seq | a->q_stride_head) & 1)
+    return set_error(B200_ERR_INVALID, "query strides must be even");
+  if ((a->out_stride_seq | a->out_stride_head) & 3)
+    return set_error(B200_ERR_INVALID, "out strides must be multiples of 4 elements");
   return B200_OK;
 }
 
@@ -555,7 +741,7 @@ size_t decode_workspace_bytes(const b200_cache_desc* c, const b200_decode_args* 
   DeviceInfo info;
   if (current_device_info(&info) != B200_OK) return 0;
   const int group = a->num_q_heads / c->num_kv_heads;
-  const int mt = group <= 16 ? 1 : (group <= 32 ? 2 : 4);
+  const int mt = decode_variant(group);
   CUtensorMap dummy;
   DecodeParams p{};
   p.group = group;
@@ -575,8 +761,8 @@ int launch_paged_decode(const b200_cache_desc* c, const b200_decode_args* a, con
   if (rc != B200_OK) return rc;
   if (!query || !block_tables || !context_lens || !out || !c->k_cache || !c->v_cache)
     return set_error(B200_ERR_INVALID, "null tensor pointer");
-  if ((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(out)) & 3)
-    return set_error(B200_ERR_INVALID, "query/out must be 4-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(query) & 3) || (reinterpret_cast<uintptr_t>(out) & 7))
+    return set_error(B200_ERR_INVALID, "query must be 4-byte and out 8-byte aligned");
   DeviceInfo info;
   rc = current_device_info(&info);
   if (rc != B200_OK) return rc;
@@ -590,7 +776,7 @@ int launch_paged_decode(const b200_cache_desc* c, const b200_decode_args* a, con
   if (rc != B200_OK) return rc;
 
   const int group = a->num_q_heads / c->num_kv_heads;
-  const int mt = group <= 16 ? 1 : (group <= 32 ? 2 : 4);
+  const int mt = decode_variant(group);
   DecodeParams p{};
   p.q = query;
   p.out = out;
@@ -686,7 +872,7 @@ int launch_paged_decode_noalloc(const b200_cache_desc* c, const b200_decode_args
   rc = current_device_info(&info);
   if (rc != B200_OK) return rc;
   const int group = a->num_q_heads / c->num_kv_heads;
-  const int mt = group <= 16 ? 1 : (group <= 32 ? 2 : 4);
+  const int mt = decode_variant(group);
   CUtensorMap unused;
   DecodeParams probe{};
   probe.group = group;

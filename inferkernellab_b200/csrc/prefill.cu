@@ -56,7 +56,8 @@ __host__ __device__ inline int prefill_smem_bytes(int num_seqs, int packed) {
   int off = S::kStages * 2 * S::kTileBytes;
   off += 3 * S::kStages * 8;                       // full, empty, masks
   off += 16;                                       // flags
-  if (packed) off += (num_seqs + 1) * 4 + kPreThreads * 4;  // tile prefix + scan scratch
+  off += kTableWindow * 4;                         // producer's block-table window
+  if (packed) off += (num_seqs + 1) * 4 + (kPreThreads / 32) * 4;  // tile prefix + scan
   return off;
 }
 
@@ -77,6 +78,8 @@ __global__ void __launch_bounds__(kPreThreads, 2)
   off += 3 * kStages * 8;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + off);
   off += 16;
+  int* table_s = reinterpret_cast<int*>(smem + off);
+  off += kTableWindow * 4;
   int* begin_s = reinterpret_cast<int*>(smem + off);
   int* scan_s = begin_s + p.num_seqs + 1;
 
@@ -105,31 +108,21 @@ __global__ void __launch_bounds__(kPreThreads, 2)
     qt = tiles - 1 - (blockIdx.x - b * tiles);  // heaviest tile of each sequence first
   } else {
     const int chunk = (B + kPreThreads - 1) / kPreThreads;
-    const int lo = tid * chunk;
+    const int lo = min(B, tid * chunk);
     const int hi = min(B, lo + chunk);
     int sum = 0;
     for (int i = lo; i < hi; ++i) {
       const long long n = p.cu_seqlens[i + 1] - p.cu_seqlens[i];
       sum += n > 0 ? static_cast<int>((n + kPreRows - 1) / kPreRows) : 0;
     }
-    scan_s[tid] = sum;
-    __syncthreads();
-    if (tid == 0) {
-      int acc = 0;
-      for (int i = 0; i < kPreThreads; ++i) {
-        const int v = scan_s[i];
-        scan_s[i] = acc;
-        acc += v;
-      }
-      begin_s[B] = acc;
-    }
-    __syncthreads();
-    int acc = scan_s[tid];
+    int total_tiles = 0;
+    int acc = block_exclusive_scan<kPreThreads>(sum, scan_s, &total_tiles);
     for (int i = lo; i < hi; ++i) {
       begin_s[i] = acc;
       const long long n = p.cu_seqlens[i + 1] - p.cu_seqlens[i];
       acc += n > 0 ? static_cast<int>((n + kPreRows - 1) / kPreRows) : 0;
     }
+    if (tid == 0) begin_s[B] = total_tiles;
     __syncthreads();
     const int x = blockIdx.x;
     if (x >= begin_s[B]) return;
@@ -167,6 +160,12 @@ __global__ void __launch_bounds__(kPreThreads, 2)
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
     }
+    TableWindow win;
+    win.ids = table_s;
+    win.row = -1;
+    win.first = 0;
+    win.count = 0;
+    const int row_pages = static_cast<int>((key_end + p.src.block_size - 1) / p.src.block_size);
     int issued = 0;
     for (int it = 0; it < n_ktiles; ++it) {
       const int s = it % kStages;
@@ -176,8 +175,8 @@ __global__ void __launch_bounds__(kPreThreads, 2)
       const int tok0 = it * kKvTile;
       const int ntok = static_cast<int>(min(static_cast<long long>(kKvTile), key_end - tok0));
       uint8_t* kdst = smem + s * 2 * S::kTileBytes;
-      issue_kv_tile<D>(&kmap, &vmap, p.src, b, hkv, tok0, ntok, kdst, kdst + S::kTileBytes,
-                       &full_bar[s], &stage_mask[s], p.err, lane);
+      issue_kv_tile<D>(&kmap, &vmap, p.src, win, b, row_pages, hkv, tok0, ntok, kdst,
+                       kdst + S::kTileBytes, &full_bar[s], &stage_mask[s], p.err, lane);
       ++issued;
     }
     if (lane == 0) drain_stages<kStages>(full_bar, issued, p.err);

@@ -230,8 +230,9 @@ def paged_decode_attention(query: torch.Tensor, cache, block_tables, context_len
         query = query.contiguous()
     if out is None:
         out = torch.empty(query.shape, dtype=query.dtype, device=query.device)
-    elif out.shape != query.shape or out.dtype != query.dtype or out.stride(-1) != 1:
-        raise ValueError("out must match the query shape and dtype")
+    elif (out.shape != query.shape or out.dtype != query.dtype or out.stride(-1) != 1
+          or out.stride(0) % 4 or out.stride(1) % 4 or out.data_ptr() % 8):
+        raise ValueError("out must match the query shape and dtype, with rows 8-byte aligned")
     desc = _cache_desc(cache)
     args = _lib.DecodeArgs(
         query.shape[0], query.shape[1], block_tables.shape[1], layer,
