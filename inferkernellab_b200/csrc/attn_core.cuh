@@ -388,6 +388,29 @@ __device__ __forceinline__ void decode_step16_T(const uint32_t (&qb)[NT][D / 16]
   const int g = lane >> 2;
   const int tq = lane & 3;
   const int mi = lane >> 3;
+  uint32_t keep0 = 0xffffffffu, keep1 = 0xffffffffu;
+  if (gmask != 0xffffu) {
+    keep0 = (((gmask >> (2 * tq)) & 1u) ? 0x0000ffffu : 0u) |
+            (((gmask >> (2 * tq + 1)) & 1u) ? 0xffff0000u : 0u);
+    keep1 = (((gmask >> (2 * tq + 8)) & 1u) ? 0x0000ffffu : 0u) |
+            (((gmask >> (2 * tq + 9)) & 1u) ? 0xffff0000u : 0u);
+  }
+  const int vrow = tok + (mi >> 1) * 8 + (lane & 7);
+  auto load_v = [&](uint32_t (&va)[D / 16][4]) {
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) {
+      const int d = i * 16 + (mi & 1) * 8;
+      const int c = d / S::kChunkElems;
+      const int dc = d - c * S::kChunkElems;
+      ldsm_x4_t(vbase + c * S::kRegionBytes + swizzle_offset(vrow * S::kChunkBytes + dc * 2, sw),
+                va[i][0], va[i][1], va[i][2], va[i][3]);
+      va[i][0] &= keep0;
+      va[i][1] &= keep0;
+      va[i][2] &= keep1;
+      va[i][3] &= keep1;
+    }
+  };
+  uint32_t va[D / 16][4];
   // ---- S^T = K Q^T, two independent accumulation chains over the k-steps ----
   float sa[NT][4], sb[NT][4];
 #pragma unroll
@@ -395,20 +418,23 @@ __device__ __forceinline__ void decode_step16_T(const uint32_t (&qb)[NT][D / 16]
 #pragma unroll
     for (int e = 0; e < 4; ++e) sa[nt][e] = sb[nt][e] = 0.f;
   const int krow = tok + (mi & 1) * 8 + (lane & 7);
+  uint32_t ka[D / 16][4];
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
     const int d = kk * 16 + (mi >> 1) * 8;
     const int c = d / S::kChunkElems;
     const int dc = d - c * S::kChunkElems;
-    uint32_t a[4];
-    ldsm_x4(kbase + c * S::kRegionBytes + swizzle_offset(krow * S::kChunkBytes + dc * 2, sw), a[0],
-            a[1], a[2], a[3]);
+    ldsm_x4(kbase + c * S::kRegionBytes + swizzle_offset(krow * S::kChunkBytes + dc * 2, sw),
+            ka[kk][0], ka[kk][1], ka[kk][2], ka[kk][3]);
+  }
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       if (kk & 1)
-        mma_16816<E>(sb[nt], a, qb[nt][kk][0], qb[nt][kk][1]);
+        mma_16816<E>(sb[nt], ka[kk], qb[nt][kk][0], qb[nt][kk][1]);
       else
-        mma_16816<E>(sa[nt], a, qb[nt][kk][0], qb[nt][kk][1]);
+        mma_16816<E>(sa[nt], ka[kk], qb[nt][kk][0], qb[nt][kk][1]);
     }
   }
   // ---- mask (keys g, g+8 of this step), scale, online softmax per head ----
@@ -443,12 +469,15 @@ __device__ __forceinline__ void decode_step16_T(const uint32_t (&qb)[NT][D / 16]
     p[nt][3] = fast_exp2(s3 - base1);
     l[nt][0] = l[nt][0] * alpha[nt][0] + (p[nt][0] + p[nt][2]);
     l[nt][1] = l[nt][1] * alpha[nt][1] + (p[nt][1] + p[nt][3]);
+    // Rescale only when some running max of this warp moved.
+    if (__any_sync(0xffffffffu, alpha[nt][0] != 1.f || alpha[nt][1] != 1.f)) {
 #pragma unroll
-    for (int i = 0; i < D / 16; ++i) {
-      oT[nt][i][0] *= alpha[nt][0];
-      oT[nt][i][1] *= alpha[nt][1];
-      oT[nt][i][2] *= alpha[nt][0];
-      oT[nt][i][3] *= alpha[nt][1];
+      for (int i = 0; i < D / 16; ++i) {
+        oT[nt][i][0] *= alpha[nt][0];
+        oT[nt][i][1] *= alpha[nt][1];
+        oT[nt][i][2] *= alpha[nt][0];
+        oT[nt][i][3] *= alpha[nt][1];
+      }
     }
   }
   // ---- P^T into B-operand layout (transpose each 8x8 half) ----
@@ -458,30 +487,13 @@ __device__ __forceinline__ void decode_step16_T(const uint32_t (&qb)[NT][D / 16]
     pb[nt][0] = movmatrix_trans(pack2<E>(p[nt][0], p[nt][1]));  // keys 0-7
     pb[nt][1] = movmatrix_trans(pack2<E>(p[nt][2], p[nt][3]));  // keys 8-15
   }
-  // V rows of keys that are not real tokens are zeroed: 0 * NaN would leak.
-  uint32_t keep0 = 0xffffffffu, keep1 = 0xffffffffu;
-  if (gmask != 0xffffu) {
-    keep0 = (((gmask >> (2 * tq)) & 1u) ? 0x0000ffffu : 0u) |
-            (((gmask >> (2 * tq + 1)) & 1u) ? 0xffff0000u : 0u);
-    keep1 = (((gmask >> (2 * tq + 8)) & 1u) ? 0x0000ffffu : 0u) |
-            (((gmask >> (2 * tq + 9)) & 1u) ? 0xffff0000u : 0u);
-  }
-  // ---- O^T += V^T P^T ----
-  const int vrow = tok + (mi >> 1) * 8 + (lane & 7);
+  // ---- O^T += V^T P^T (V rows of keys that are not real tokens are zeroed:
+  // 0 * NaN would leak) ----
+  load_v(va);
 #pragma unroll
   for (int i = 0; i < D / 16; ++i) {
-    const int d = i * 16 + (mi & 1) * 8;
-    const int c = d / S::kChunkElems;
-    const int dc = d - c * S::kChunkElems;
-    uint32_t a[4];
-    ldsm_x4_t(vbase + c * S::kRegionBytes + swizzle_offset(vrow * S::kChunkBytes + dc * 2, sw),
-              a[0], a[1], a[2], a[3]);
-    a[0] &= keep0;
-    a[1] &= keep0;
-    a[2] &= keep1;
-    a[3] &= keep1;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) mma_16816<E>(oT[nt][i], a, pb[nt][0], pb[nt][1]);
+    for (int nt = 0; nt < NT; ++nt) mma_16816<E>(oT[nt][i], va[i], pb[nt][0], pb[nt][1]);
   }
 }
 

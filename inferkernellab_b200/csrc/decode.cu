@@ -383,20 +383,26 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       const uint64_t tmask = stage_mask[s];
       const uint32_t kbase = smem_base + s * L.stage_bytes;
       const uint32_t vbase = kbase + S::kTileBytes;
-#pragma unroll
-      for (int gi = 0; gi < kGroups16; ++gi) {
-        const int tok = slice * kTokPerWarp + gi * 16;  // first tile row of this 16-key group
+      if constexpr (kTrans) {
+        const int tok = slice * kTokPerWarp;  // one 16-key group per warp
         const uint32_t gmask = static_cast<uint32_t>(tmask >> tok) & 0xffffu;
-        if (gmask == 0) continue;
-        if constexpr (kTrans)
+        if (gmask != 0)
           decode_step16_T<E, D, NT>(qb, oT, m_t, l_t, kbase, vbase, tok, gmask, p.scale_log2, sw,
                                     lane);
-        else
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[s]);
+      } else {
+#pragma unroll
+        for (int gi = 0; gi < kGroups16; ++gi) {
+          const int tok = slice * kTokPerWarp + gi * 16;  // first tile row of this 16-key group
+          const uint32_t gmask = static_cast<uint32_t>(tmask >> tok) & 0xffffu;
+          if (gmask == 0) continue;
           attend16<E, D, false>(qf, o, m_r, l_r, kbase, vbase, tok, gmask, 0, 0, 0,
                                 p.scale_log2, sw, lane);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[s]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[s]);
     }
 
     // ---- segment end: merge the token slices, then finish or publish ----

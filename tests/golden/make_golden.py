@@ -14,7 +14,9 @@ torch, CPU) and records, for seeded inputs, what the reference computes:
 * ``prefill_*.npz``      -- ``paged_prefill_attention_sdpa`` (``attention.py:230-321``);
 * ``append.npz``         -- ``PagedKVCache.write_slots`` (``cache.py:156-189``);
 * ``runtime_events.json``-- ``InferenceRuntime`` hook traces (``runtime.py:65-104``)
-                            and ``TokenBudgetScheduler`` packing (``scheduler.py:50-84``).
+                            and ``TokenBudgetScheduler`` packing (``scheduler.py:50-84``);
+* ``synthetic_decoder.json`` -- ``SyntheticDecodeRunner`` tokens and logits
+                            (``decode.py:152-592``), float32 on CPU.
 
 The GPU box has no reference checkout, so only the resulting ``.npz``/``.json``
 files travel; nothing at test time imports the reference.
@@ -241,6 +243,31 @@ def _runtime_traces(ikl):
     (HERE / "runtime_events.json").write_text(json.dumps(traces, indent=1) + "\n")
 
 
+def _synthetic_cases(ikl):
+    """Reference SyntheticDecodeRunner (decode.py:152-592), float32 on CPU."""
+    dec = ikl["decode"]
+    cases = {
+        "ref_small": dict(cfg=dict(vocab_size=32, num_heads=4, num_kv_heads=2, head_dim=8,
+                                   block_size=4, seed=19, max_num_seqs=2,
+                                   max_num_batched_tokens=4),
+                          prompts=[[1, 2, 3], [7, 8, 9, 10]], max_new=3),
+        "gqa_d64": dict(cfg=dict(vocab_size=256, num_heads=32, num_kv_heads=8, head_dim=64,
+                                 block_size=16, seed=0, max_num_seqs=8,
+                                 max_num_batched_tokens=64),
+                        prompts=[[(7 * i + 3 * j) % 256 for j in range(n)]
+                                 for i, n in enumerate([5, 17, 40, 1, 33])], max_new=6),
+    }
+    out = {}
+    for name, c in cases.items():
+        cfg = dec.SyntheticDecoderConfig(dtype=torch.float32, device="cpu",
+                                         backend="paged_reference", **c["cfg"])
+        res = dec.SyntheticDecodeRunner(cfg, c["prompts"], max_new_tokens=c["max_new"]).run()
+        out[name] = {"cfg": c["cfg"], "prompts": c["prompts"], "max_new": c["max_new"],
+                     "generated": [list(t) for t in res.generated_tokens],
+                     "logits": [l.tolist() for l in res.logits]}
+    (HERE / "synthetic_decoder.json").write_text(json.dumps(out) + "\n")
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--reference", required=True, help="path of the reference project checkout")
@@ -249,13 +276,14 @@ def main() -> None:
     import importlib
 
     ikl = {m: importlib.import_module(f"inferkernellab.{m}")
-           for m in ("cache", "attention", "runtime", "scheduler")}
+           for m in ("cache", "attention", "runtime", "scheduler", "decode")}
     torch.set_num_threads(4)
     _slot_cases(ikl)
     _decode_cases(ikl)
     _prefill_cases(ikl)
     _append_case(ikl)
     _runtime_traces(ikl)
+    _synthetic_cases(ikl)
     print("golden fixtures written to", HERE)
 
 

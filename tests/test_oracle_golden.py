@@ -75,3 +75,24 @@ def test_bf16_round_trip_is_exact_and_rounds_to_nearest_even():
     # 1 + 2^-8 is exactly between two bf16 values: ties go to the even mantissa (1.0).
     assert oracle.f32_to_bf16_bits(np.array([1.0 + 2 ** -8], np.float32))[0] == 0x3F80
     assert oracle.f32_to_bf16_bits(np.array([1.0 + 3 * 2 ** -8], np.float32))[0] == 0x3F82
+
+
+def test_synthetic_decoder_oracle_matches_reference():
+    """The numpy synthetic-decoder restatement reproduces the reference runner's
+    float32 logits and greedy tokens (tests/golden/synthetic_decoder.json)."""
+    import json
+
+    from oracle import synthetic_ref
+
+    data = json.loads((GOLDEN / "synthetic_decoder.json").read_text())
+    for name, case in data.items():
+        cfg = case["cfg"]
+        weights = synthetic_ref.make_weights(cfg["vocab_size"], cfg["num_heads"],
+                                             cfg["num_kv_heads"], cfg["head_dim"], cfg["seed"])
+        logits = synthetic_ref.decode_logits(weights, case["prompts"], case["generated"],
+                                             cfg["num_heads"], cfg["num_kv_heads"], cfg["head_dim"])
+        assert len(logits) == case["max_new"]
+        for step, (got, want) in enumerate(zip(logits, case["logits"])):
+            np.testing.assert_allclose(got, np.asarray(want, np.float32), atol=2e-6, rtol=1e-5,
+                                       err_msg=f"{name} step {step}")
+            assert got.argmax(-1).tolist() == [g[step] for g in case["generated"]]
