@@ -1,0 +1,486 @@
+"""Transformers Llama decoder over the paged KV cache, on the b200 kernels.
+
+Mirror of the reference's ``LlamaPagedDecodeRunner`` / ``LlamaPagedRunResult``
+(reference ``src/inferkernellab/hf_benchmark.py:88-695``) for backend
+``"b200_paged"`` / append ``"b200"``.  Every non-attention op is the model's own
+Transformers module (RMSNorm, q/k/v/o projections, rotary embedding, SiLU MLP,
+final norm, lm_head), applied exactly as the reference does, so logits differ
+from the eager model only through attention arithmetic.  Attention-side work is
+on the sm_100a kernels:
+
+* batched prefill is *packed*: the scheduled ranges of a budget batch are
+  concatenated (no padding rows, unlike the reference's ``_prefill_batch``
+  ``:522-547``), slots and ``cu_seqlens`` come from one device
+  ``build_slot_mapping`` launch per batch, K/V go in with ``append_kv`` and the
+  causal attention runs in ``paged_prefill_attention_varlen``;
+* decode appends each request's new K/V and runs ``paged_decode_attention``;
+  the step's slots and lengths are built once and reused by all layers.
+
+Multi-GPU: requests are partitioned over ranks by the caller; each rank runs its
+own runner (own block pool) and passes ``token_exchange`` -- e.g.
+``allgather_token_exchange`` -- which all-gathers the sampled token ids of every
+decode step over NCCL (the only collective on this path).
+"""
+
+from __future__ import annotations
+
+import math
+import time
+from collections.abc import Callable, Sequence
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+
+from .cache import PagedKVCache
+from .decode import DeviceBlockTables, _percentile
+from .ops import append_kv, build_slot_mapping, paged_decode_attention, paged_prefill_attention_varlen
+from .runtime import InferenceRuntime
+from .scheduler import InferenceRequest, TokenBudgetScheduler
+
+
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    first, second = x[..., : x.shape[-1] // 2], x[..., x.shape[-1] // 2:]
+    return torch.cat((-second, first), dim=-1)
+
+
+def _apply_rotary(query, key, cos, sin):
+    """Rotary embedding as the reference applies it (hf_benchmark.py:69-85).
+
+    ``query``/``key`` ``[..., heads, D]``; ``cos``/``sin`` broadcast over heads."""
+    cos = cos.unsqueeze(-2)
+    sin = sin.unsqueeze(-2)
+    return query * cos + _rotate_half(query) * sin, key * cos + _rotate_half(key) * sin
+
+
+@dataclass(frozen=True)
+class LlamaPagedRunResult:
+    backend: str
+    append_backend: str
+    prompt_lengths: tuple[int, ...]
+    max_new_tokens: int
+    generated_tokens: tuple[tuple[int, ...], ...]
+    prompt_logits: torch.Tensor
+    decode_logits: tuple[torch.Tensor, ...]
+    prefill_wall_ms: float
+    decode_step_wall_ms: tuple[float, ...]
+    ttft_wall_ms: float
+    tpot_wall_ms: float
+    peak_memory_allocated_bytes: int
+    peak_kv_memory_bytes: int
+    used_blocks_peak: int
+    cache_released: bool
+    prefill_step_wall_ms: tuple[float, ...] = ()
+    prefill_mode: str = "token"
+    prefill_batch_count: int = 0
+    prefill_tokens: int = 0
+    prefill_padding_tokens: int = 0
+    token_logprobs: tuple[tuple[float, ...], ...] = ()
+    sampling_logprobs: tuple[tuple[float, ...], ...] = ()
+    finish_reasons: tuple[str, ...] = ()
+
+    @property
+    def decode_p50_ms(self) -> float:
+        return _percentile(self.decode_step_wall_ms, 0.50)
+
+    @property
+    def decode_p95_ms(self) -> float:
+        return _percentile(self.decode_step_wall_ms, 0.95)
+
+    @property
+    def prefill_p50_ms(self) -> float:
+        return _percentile(self.prefill_step_wall_ms, 0.50)
+
+    @property
+    def prefill_p95_ms(self) -> float:
+        return _percentile(self.prefill_step_wall_ms, 0.95)
+
+
+TokenExchange = Callable[[torch.Tensor], None]
+
+
+class LlamaPagedDecodeRunner:
+    """Run a Transformers Llama one token at a time over the paged cache (b200 backend)."""
+
+    def __init__(self, model: Any, prompts: Sequence[Sequence[int]], *, max_new_tokens: int,
+                 backend: str = "b200_paged", block_size: int = 16, append_backend: str = "b200",
+                 max_num_batched_tokens: int = 2048, prefill_mode: str = "batched",
+                 temperature: float = 0.0, top_p: float = 1.0, seed: int = 2026,
+                 eos_token_ids: Sequence[int] | None = None,
+                 token_exchange: TokenExchange | None = None, collect_logits: bool = True):
+        if not prompts:
+            raise ValueError("at least one prompt is required")
+        if max_new_tokens <= 0:
+            raise ValueError("max_new_tokens must be positive")
+        if block_size <= 0 or max_num_batched_tokens <= 0:
+            raise ValueError("block-size and max-num-batched-tokens must be positive")
+        if backend != "b200_paged":
+            raise ValueError(f"unsupported backend: {backend}")
+        if append_backend != "b200":
+            raise ValueError(f"unsupported append backend: {append_backend}")
+        if prefill_mode not in {"batched", "token"}:
+            raise ValueError("prefill_mode must be batched or token")
+        if (not math.isfinite(temperature) or temperature < 0 or not math.isfinite(top_p)
+                or not 0 < top_p <= 1):
+            raise ValueError("temperature must be non-negative and top_p must be in (0, 1]")
+        self.model = model
+        param = next(model.parameters())
+        self.device, self.dtype = param.device, param.dtype
+        if self.device.type != "cuda":
+            raise ValueError("the b200 backend needs the model on a CUDA device")
+        self.prompts = tuple(tuple(int(t) for t in p) for p in prompts)
+        if any(not p for p in self.prompts):
+            raise ValueError("prompts must be non-empty")
+        vocab = int(model.config.vocab_size)
+        if any(t < 0 or t >= vocab for p in self.prompts for t in p):
+            raise ValueError("prompt token is outside the configured vocabulary")
+        self.backend, self.append_backend, self.prefill_mode = backend, append_backend, prefill_mode
+        self.max_new_tokens = max_new_tokens
+        self.temperature, self.top_p = temperature, top_p
+        self.eos_token_ids = set(eos_token_ids or ())
+        if any(t < 0 or t >= vocab for t in self.eos_token_ids):
+            raise ValueError("EOS token id is outside the configured vocabulary")
+        self.token_exchange = token_exchange
+        self.collect_logits = collect_logits
+        self.prompt_lengths = tuple(len(p) for p in self.prompts)
+        cfg = model.config
+        self.num_layers = int(cfg.num_hidden_layers)
+        self.num_heads = int(cfg.num_attention_heads)
+        self.num_kv_heads = int(cfg.num_key_value_heads)
+        self.head_dim = int(getattr(cfg, "head_dim", None) or cfg.hidden_size // self.num_heads)
+        if self.num_heads % self.num_kv_heads != 0:
+            raise ValueError("num_attention_heads must be divisible by num_key_value_heads")
+        total_blocks = sum(-(-(n + max_new_tokens) // block_size) for n in self.prompt_lengths)
+        self.cache = PagedKVCache(total_blocks, block_size, self.num_kv_heads, self.head_dim,
+                                  num_layers=self.num_layers, dtype=self.dtype, device=self.device)
+        scheduler = TokenBudgetScheduler(max_num_seqs=len(self.prompts),
+                                         max_num_batched_tokens=max_num_batched_tokens)
+        self.runtime = InferenceRuntime(
+            self.cache, scheduler,
+            prefill_fn=self._prefill if prefill_mode == "token" else None,
+            prefill_batch_fn=self._prefill_batch if prefill_mode == "batched" else None,
+            decode_fn=self._decode)
+        self.requests = [self.runtime.submit(rid, len(p), max_new_tokens)
+                         for rid, p in enumerate(self.prompts)]
+        width = max(1, max(-(-(n + max_new_tokens) // block_size) for n in self.prompt_lengths))
+        self.meta = DeviceBlockTables(len(self.requests), width, self.device)
+        self._prompt_logits: dict[int, torch.Tensor] = {}
+        self._next_logits: dict[int, torch.Tensor] = {}
+        self._decode_logits: list[torch.Tensor] = []
+        self._generated: dict[int, list[int]] = {r.request_id: [] for r in self.requests}
+        self._token_logprobs: dict[int, list[float]] = {r.request_id: [] for r in self.requests}
+        self._sampling_logprobs: dict[int, list[float]] = {r.request_id: [] for r in self.requests}
+        self._finish_reasons = {r.request_id: "length" for r in self.requests}
+        self._generators = {}
+        for r in self.requests:
+            gen = torch.Generator(device=self.device)
+            gen.manual_seed(seed + r.request_id)
+            self._generators[r.request_id] = gen
+        self._has_run = False
+
+    # ------------------------------------------------------------------ layers
+    def _layer_qkv(self, layer, hidden, cos, sin, tokens: int):
+        attn = layer.self_attn
+        q = attn.q_proj(hidden).view(tokens, self.num_heads, self.head_dim)
+        k = attn.k_proj(hidden).view(tokens, self.num_kv_heads, self.head_dim)
+        v = attn.v_proj(hidden).view(tokens, self.num_kv_heads, self.head_dim)
+        q, k = _apply_rotary(q, k, cos, sin)
+        return q.contiguous(), k.contiguous(), v.contiguous()
+
+    def _layer_tail(self, layer, residual, attended, tokens: int):
+        hidden = residual + layer.self_attn.o_proj(attended.reshape(tokens, -1))
+        residual = hidden
+        hidden = layer.post_attention_layernorm(hidden)
+        hidden = layer.mlp.down_proj(layer.mlp.act_fn(layer.mlp.gate_proj(hidden))
+                                     * layer.mlp.up_proj(hidden))
+        return residual + hidden
+
+    def _forward(self, token_ids: torch.Tensor, positions: torch.Tensor, attend) -> torch.Tensor:
+        """Shared layer loop on a flat token batch ``[N]``; returns hidden ``[N, H]``."""
+        n = token_ids.shape[0]
+        hidden = self.model.model.embed_tokens(token_ids.to(torch.long))
+        cos, sin = self.model.model.rotary_emb(hidden.unsqueeze(0), positions.view(1, -1))
+        cos, sin = cos[0], sin[0]
+        for index, layer in enumerate(self.model.model.layers):
+            residual = hidden
+            hidden = layer.input_layernorm(hidden)
+            q, k, v = self._layer_qkv(layer, hidden, cos, sin, n)
+            attended = attend(index, q, k, v)
+            hidden = self._layer_tail(layer, residual, attended, n)
+        return self.model.model.norm(hidden)
+
+    def _forward_decode(self, token_ids, requests, positions: Sequence[int]) -> torch.Tensor:
+        self.meta.sync(requests)
+        bs, nb = self.cache.layout.block_size, self.cache.layout.num_blocks
+        starts = torch.tensor([list(positions), [p + 1 for p in positions]], dtype=torch.int32)
+        starts = starts.to(self.device, non_blocking=True)
+        tables = self.meta.rows(requests)
+        slots, _ = build_slot_mapping(tables, starts[0], starts[1], block_size=bs, num_blocks=nb,
+                                      total_tokens=len(positions), with_cu_seqlens=False)
+        lens = starts[1]
+        pos = starts[0].to(torch.long)
+
+        def attend(layer, q, k, v):
+            append_kv(k, v, self.cache, slots, layer=layer)
+            return paged_decode_attention(q, self.cache, tables, lens, layer=layer,
+                                          validate_inputs=False)
+
+        hidden = self._forward(token_ids, pos, attend)
+        return self.model.lm_head(hidden)
+
+    def _forward_prefill_packed(self, requests, starts, ends) -> torch.Tensor:
+        """Packed ranges of one budget batch; returns hidden of every token ``[sum T, H]``."""
+        self.meta.sync(requests)
+        bs, nb = self.cache.layout.block_size, self.cache.layout.num_blocks
+        meta = torch.tensor([list(starts), list(ends)], dtype=torch.int32).to(self.device,
+                                                                            non_blocking=True)
+        total = int(sum(e - s for s, e in zip(starts, ends)))
+        tables = self.meta.rows(requests)
+        slots, cu = build_slot_mapping(tables, meta[0], meta[1], block_size=bs, num_blocks=nb,
+                                       total_tokens=total)
+        ids = torch.tensor([t for r, s, e in zip(requests, starts, ends)
+                            for t in self.prompts[r.request_id][s:e]], dtype=torch.long)
+        pos = torch.tensor([p for s, e in zip(starts, ends) for p in range(s, e)],
+                           dtype=torch.long)
+        ids = ids.to(self.device, non_blocking=True)
+        pos = pos.to(self.device, non_blocking=True)
+
+        def attend(layer, q, k, v):
+            append_kv(k, v, self.cache, slots, layer=layer)
+            return paged_prefill_attention_varlen(q, self.cache, tables, cu, meta[0], meta[1],
+                                                  layer=layer)
+
+        return self._forward(ids, pos, attend)
+
+    # ------------------------------------------------------------------- hooks
+    def _prefill(self, request: InferenceRequest, start: int, end: int) -> None:
+        hidden = self._forward_prefill_packed((request,), (start,), (end,))
+        if end == len(self.prompts[request.request_id]):
+            logits = self.model.lm_head(hidden[-1:])[0].detach()
+            self._prompt_logits[request.request_id] = logits
+            self._next_logits[request.request_id] = logits
+
+    def _prefill_batch(self, requests, starts, ends) -> None:
+        lengths = [int(e) - int(s) for s, e in zip(starts, ends)]
+        if not requests or any(n <= 0 for n in lengths):
+            raise ValueError("prefill batch must contain non-empty ranges")
+        hidden = self._forward_prefill_packed(requests, starts, ends)
+        last, rows, offset = [], [], 0
+        for request, end, n in zip(requests, ends, lengths):
+            offset += n
+            if end == len(self.prompts[request.request_id]):
+                last.append(offset - 1)
+                rows.append(request.request_id)
+        if last:
+            logits = self.model.lm_head(hidden[torch.tensor(last, device=self.device)]).detach()
+            for rid, row in zip(rows, logits):
+                self._prompt_logits[rid] = row
+                self._next_logits[rid] = row
+
+    def _sample_token(self, logits: torch.Tensor, generator: torch.Generator):
+        """Temperature / top-p sampling as the reference does (hf_benchmark.py:581-605)."""
+        values = logits.float()
+        if self.temperature > 0:
+            values = values / self.temperature
+        policy_logprobs = torch.log_softmax(values, dim=-1)
+        if self.top_p < 1.0:
+            sorted_logits, sorted_indices = torch.sort(values, descending=True)
+            sorted_probs = torch.softmax(sorted_logits, dim=-1)
+            remove = sorted_probs.cumsum(dim=-1) - sorted_probs > self.top_p
+            sorted_logits = sorted_logits.masked_fill(remove, float("-inf"))
+            values = torch.full_like(values, float("-inf")).scatter(-1, sorted_indices,
+                                                                     sorted_logits)
+        log_probs = torch.log_softmax(values, dim=-1)
+        if self.temperature == 0:
+            token = values.argmax(dim=-1)
+        else:
+            token = torch.multinomial(log_probs.exp(), num_samples=1, generator=generator).squeeze(-1)
+        return (token, policy_logprobs.gather(-1, token.view(1)).squeeze(0),
+                log_probs.gather(-1, token.view(1)).squeeze(0))
+
+    def _decode(self, requests: tuple[InferenceRequest, ...]) -> None:
+        used = torch.stack([self._next_logits[r.request_id] for r in requests], dim=0)
+        sampled = None
+        if self.temperature == 0 and not self.eos_token_ids:
+            next_tokens = used.argmax(dim=-1).to(torch.long)
+        else:
+            sampled = [self._sample_token(used[i], self._generators[r.request_id])
+                       for i, r in enumerate(requests)]
+            next_tokens = torch.stack([s[0] for s in sampled]).to(torch.long)
+        if self.token_exchange is not None:
+            self.token_exchange(next_tokens)
+        positions = [r.prompt_tokens + r.generated_tokens for r in requests]
+        next_logits = self._forward_decode(next_tokens, requests, positions)
+        if self.collect_logits:
+            self._decode_logits.append(used.detach().float().cpu())
+        tokens = next_tokens.tolist()
+        for row, request in enumerate(requests):
+            token = int(tokens[row])
+            self._generated[request.request_id].append(token)
+            if sampled is not None:
+                self._token_logprobs[request.request_id].append(float(sampled[row][1].item()))
+                self._sampling_logprobs[request.request_id].append(float(sampled[row][2].item()))
+            if token in self.eos_token_ids:
+                self._finish_reasons[request.request_id] = "eos"
+                request.max_new_tokens = request.generated_tokens + 1
+            self._next_logits[request.request_id] = next_logits[row].detach()
+
+    # --------------------------------------------------------------------- run
+    def _timed_step(self):
+        started = time.perf_counter()
+        batch = self.runtime.step()
+        torch.cuda.synchronize(self.device)
+        return batch, (time.perf_counter() - started) * 1000
+
+    def run(self) -> LlamaPagedRunResult:
+        if self._has_run:
+            raise RuntimeError("a LlamaPagedDecodeRunner instance can only be run once")
+        self._has_run = True
+        torch.cuda.reset_peak_memory_stats(self.device)
+        prefill_ms, prefill_steps, decode_ms = 0.0, [], []
+        used_peak = self.cache.allocator.num_used_blocks
+        with torch.inference_mode():
+            while self.runtime.scheduler.waiting or self.runtime.scheduler.running:
+                batch, elapsed = self._timed_step()
+                used_peak = max(used_peak, self.cache.allocator.num_used_blocks)
+                if batch.phase == "prefill":
+                    prefill_ms += elapsed
+                    prefill_steps.append(elapsed)
+                elif batch.phase == "decode":
+                    decode_ms.append(elapsed)
+                else:
+                    raise RuntimeError("scheduler became idle before all requests finished")
+        cache_released = self.cache.allocator.num_used_blocks == 0
+        if len(self._prompt_logits) != len(self.requests):
+            raise RuntimeError("prefill did not produce one final logits tensor per request")
+        generated = tuple(tuple(self._generated[r.request_id]) for r in self.requests)
+        if any(not t or len(t) > self.max_new_tokens for t in generated):
+            raise RuntimeError("decoder finished with an invalid generated sequence length")
+        element = torch.tensor([], dtype=self.dtype).element_size()
+        lay = self.cache.layout
+        peak_kv = (used_peak * lay.block_size * lay.num_layers * lay.num_kv_heads * lay.head_dim
+                   * 2 * element)
+        return LlamaPagedRunResult(
+            backend=self.backend, append_backend=self.append_backend,
+            prompt_lengths=self.prompt_lengths, max_new_tokens=self.max_new_tokens,
+            generated_tokens=generated,
+            prompt_logits=torch.stack([self._prompt_logits[r.request_id]
+                                       for r in self.requests]).float().cpu(),
+            decode_logits=tuple(self._decode_logits), prefill_wall_ms=prefill_ms,
+            prefill_step_wall_ms=tuple(prefill_steps), prefill_mode=self.prefill_mode,
+            prefill_batch_count=len(prefill_steps), prefill_tokens=sum(self.prompt_lengths),
+            prefill_padding_tokens=0,
+            token_logprobs=tuple(tuple(self._token_logprobs[r.request_id]) for r in self.requests),
+            sampling_logprobs=tuple(tuple(self._sampling_logprobs[r.request_id])
+                                    for r in self.requests),
+            finish_reasons=tuple(self._finish_reasons[r.request_id] for r in self.requests),
+            decode_step_wall_ms=tuple(decode_ms), ttft_wall_ms=prefill_ms + decode_ms[0],
+            tpot_wall_ms=sum(decode_ms) / len(decode_ms),
+            peak_memory_allocated_bytes=int(torch.cuda.max_memory_allocated(self.device)),
+            peak_kv_memory_bytes=peak_kv, used_blocks_peak=used_peak,
+            cache_released=cache_released and self.cache.allocator.num_used_blocks == 0)
+
+
+# ------------------------------------------------------------------ helpers
+
+def load_random_llama(*, vocab_size: int, hidden_size: int, intermediate_size: int,
+                      num_layers: int, num_attention_heads: int, num_kv_heads: int,
+                      max_position_embeddings: int, rope_theta: float, seed: int,
+                      device: torch.device | str = "cuda", dtype: torch.dtype = torch.bfloat16,
+                      init_on_device: bool = False):
+    """Random-init ``LlamaForCausalLM`` like the reference's ``_load_model`` (hf_benchmark.py:698-745).
+
+    ``init_on_device=False`` reproduces the reference bit for bit (CPU float32
+    init after ``torch.manual_seed(seed)``, then cast); ``True`` initialises on
+    the GPU in ``dtype`` (same N(0, 0.02) scheme, different random stream),
+    which is the practical way to build an 8B-parameter model.
+    """
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    config = LlamaConfig(vocab_size=vocab_size, hidden_size=hidden_size,
+                         intermediate_size=intermediate_size, num_hidden_layers=num_layers,
+                         num_attention_heads=num_attention_heads, num_key_value_heads=num_kv_heads,
+                         max_position_embeddings=max_position_embeddings, rope_theta=rope_theta,
+                         attention_bias=False, mlp_bias=False, tie_word_embeddings=False)
+    config._attn_implementation = "eager"
+    torch.manual_seed(seed)
+    if init_on_device:
+        previous = torch.get_default_dtype()
+        torch.set_default_dtype(dtype)
+        try:
+            with torch.device(device):
+                model = LlamaForCausalLM(config)
+        finally:
+            torch.set_default_dtype(previous)
+    else:
+        model = LlamaForCausalLM(config)
+    model.config._attn_implementation = "eager"
+    model = model.to(device=device, dtype=dtype).eval()
+    for parameter in model.parameters():
+        parameter.requires_grad_(False)
+    return model
+
+
+def eager_reference_logits(model, prompts, generated_tokens) -> tuple[torch.Tensor, ...]:
+    """Full-sequence eager forward per step, the reference's oracle (hf_benchmark.py:764-779)."""
+    device = next(model.parameters()).device
+    outputs = []
+    for step in range(len(generated_tokens[0]) + 1):
+        with torch.inference_mode():
+            rows = []
+            for prompt, tokens in zip(prompts, generated_tokens):
+                sequence = tuple(prompt) + tuple(tokens[:step])
+                ids = torch.tensor([sequence], dtype=torch.long, device=device)
+                rows.append(model(ids, use_cache=False, return_dict=True).logits[0, -1, :])
+        outputs.append(torch.stack(rows).float().cpu())
+    return tuple(outputs)
+
+
+def correctness(model, prompts, result: LlamaPagedRunResult) -> dict:
+    """Logit error and greedy-token match against the eager model (hf_benchmark.py:782-823)."""
+    refs = eager_reference_logits(model, prompts, result.generated_tokens)
+    prompt_err = float((result.prompt_logits.float() - refs[0].float()).abs().max())
+    decode_errs = [float((a.float() - b.float()).abs().max())
+                   for a, b in zip(result.decode_logits, refs[:-1])]
+    errs = [prompt_err, *decode_errs]
+    ours = torch.stack([l.argmax(-1) for l in result.decode_logits], dim=1)
+    theirs = torch.stack([l.argmax(-1) for l in refs[:-1]], dim=1)
+    matches = int((ours == theirs).sum())
+    dtype = next(model.parameters()).dtype
+    tol = 3e-2 if dtype == torch.bfloat16 else 5e-3 if dtype == torch.float16 else 1e-4
+    # Smallest top-2 margin of the eager logits where the tokens disagree (0 if none).
+    flips = [(float(r.topk(2).values[0] - r.topk(2).values[1]))
+             for step, ref in enumerate(refs[:-1]) for i, r in enumerate(ref)
+             if int(ours[i, step]) != int(theirs[i, step])]
+    return {"logits_max_error": max(errs), "prefill_logits_max_error": errs[0],
+            "decode_logits_max_error": max(errs[1:]) if len(errs) > 1 else 0.0,
+            "token_match_rate": matches / max(int(theirs.numel()), 1), "token_matches": matches,
+            "token_count": int(theirs.numel()), "logits_tolerance": tol,
+            "flip_margins": flips,
+            "status": "ok" if max(errs) <= tol and matches == theirs.numel() else "failed",
+            "oracle": "Transformers Llama eager full-sequence path"}
+
+
+def allgather_token_exchange(group=None, max_local: int | None = None) -> TokenExchange:
+    """NCCL all-gather of every rank's sampled token ids (one collective per decode step).
+
+    Returns a callable for ``LlamaPagedDecodeRunner(token_exchange=...)``; the
+    gathered ids of the last step are kept in ``callable.last`` (``[world, max_local]``,
+    ``-1`` = padding).
+    """
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    state = {"buf": None}
+
+    def exchange(tokens: torch.Tensor) -> None:
+        width = max_local or tokens.numel()
+        local = torch.full((width,), -1, dtype=torch.int32, device=tokens.device)
+        local[: tokens.numel()] = tokens.to(torch.int32)
+        if state["buf"] is None or state["buf"].shape[1] != width:
+            state["buf"] = torch.empty((world, width), dtype=torch.int32, device=tokens.device)
+        dist.all_gather_into_tensor(state["buf"], local, group=group)
+        exchange.last = state["buf"]
+
+    exchange.last = None
+    return exchange

@@ -1,0 +1,91 @@
+"""Transformers Llama over the paged cache on the b200 kernels, end to end.
+
+Mirrors the reference's tests/test_hf_benchmark.py: random-init Llama models
+built exactly like the reference's _load_model (CPU float32 init after
+torch.manual_seed, then cast), decoded greedily through the runtime, and
+checked against the Transformers eager full-sequence forward (the reference's
+own oracle, hf_benchmark.py:764-823) with its logit tolerances (bf16 3e-2,
+fp16 5e-3) and greedy-token match.
+"""
+
+import pytest
+import torch
+
+from inferkernellab_b200.llama import LlamaPagedDecodeRunner, correctness, load_random_llama
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(dtype, num_kv_heads=2, num_layers=2, hidden=64, heads=4, vocab=128, seed=2026):
+    return load_random_llama(vocab_size=vocab, hidden_size=hidden, intermediate_size=2 * hidden,
+                             num_layers=num_layers, num_attention_heads=heads,
+                             num_kv_heads=num_kv_heads, max_position_embeddings=256,
+                             rope_theta=10_000.0, seed=seed, device="cuda", dtype=dtype)
+
+
+def _prompts(batch, length, vocab, seed=2026):
+    # The reference's arithmetic prompt generator (hf_benchmark.py:748-761).
+    base = torch.arange(length, dtype=torch.long)
+    return tuple(tuple(((base + seed + row * 17) % vocab).tolist()) for row in range(batch))
+
+
+def _assert_ok(report):
+    tol = report["logits_tolerance"]
+    assert report["logits_max_error"] <= tol, report
+    # Greedy tokens match, except possible flips where the eager top-2 margin is tiny.
+    assert report["token_match_rate"] == 1.0 or all(m < 2 * tol for m in report["flip_margins"]), report
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+@pytest.mark.parametrize("num_kv_heads,num_layers", [(4, 1), (2, 2), (1, 2)])
+def test_llama_runner_matches_eager(dtype, num_kv_heads, num_layers):
+    model = _model(dtype, num_kv_heads=num_kv_heads, num_layers=num_layers)
+    prompts = _prompts(2, 5, 128)
+    result = LlamaPagedDecodeRunner(model, prompts, max_new_tokens=3, block_size=4).run()
+    _assert_ok(correctness(model, prompts, result))
+    assert result.cache_released
+    assert result.decode_p95_ms >= result.decode_p50_ms > 0
+
+
+def test_llama_runner_ragged_batched_prefill_ignores_nan_slots():
+    """Reference test_hf_benchmark.py:101-123 with the cache poisoned by NaN."""
+    model = _model(torch.bfloat16)
+    prompts = ((1, 2, 3, 4, 5, 9, 11, 3, 2), (6, 7, 8), tuple(range(20, 57)))
+    runner = LlamaPagedDecodeRunner(model, prompts, max_new_tokens=3, block_size=4,
+                                    max_num_batched_tokens=16)
+    runner.cache.k.fill_(float("nan"))
+    runner.cache.v.fill_(float("nan"))
+    result = runner.run()
+    _assert_ok(correctness(model, prompts, result))
+    assert result.prefill_batch_count >= 2  # the budget chunks the long prompt
+    assert result.cache_released
+
+
+def test_llama_token_and_batched_prefill_agree():
+    model = _model(torch.float16)
+    prompts = _prompts(3, 9, 128)
+    token = LlamaPagedDecodeRunner(model, prompts, max_new_tokens=3, block_size=4,
+                                   prefill_mode="token").run()
+    batched = LlamaPagedDecodeRunner(model, prompts, max_new_tokens=3, block_size=4,
+                                     prefill_mode="batched").run()
+    assert token.generated_tokens == batched.generated_tokens
+    assert torch.allclose(token.prompt_logits, batched.prompt_logits, atol=5e-3, rtol=0)
+
+
+def test_llama_runner_head_dim_128_gqa_long_prompts():
+    model = _model(torch.bfloat16, num_kv_heads=2, num_layers=2, hidden=512, heads=4)
+    prompts = tuple(tuple((7 * i + j) % 128 for j in range(n)) for i, n in enumerate([130, 64, 7]))
+    result = LlamaPagedDecodeRunner(model, prompts, max_new_tokens=4, block_size=16,
+                                    max_num_batched_tokens=128).run()
+    _assert_ok(correctness(model, prompts, result))
+
+
+def test_llama_sampling_is_seeded():
+    model = _model(torch.bfloat16)
+    prompts = _prompts(2, 6, 128)
+    a = LlamaPagedDecodeRunner(model, prompts, max_new_tokens=4, block_size=4, temperature=0.8,
+                               top_p=0.9, seed=7).run()
+    b = LlamaPagedDecodeRunner(model, prompts, max_new_tokens=4, block_size=4, temperature=0.8,
+                               top_p=0.9, seed=7).run()
+    assert a.generated_tokens == b.generated_tokens
+    assert all(len(x) == 4 for x in a.token_logprobs)

@@ -9,6 +9,7 @@ import json
 from pathlib import Path
 
 import pytest
+import torch
 
 from inferkernellab_b200 import InferenceRequest, InferenceRuntime, PagedKVCache, TokenBudgetScheduler
 
@@ -98,3 +99,33 @@ def test_scheduler_marks_finished_and_validates():
         scheduler.add(request)
     with pytest.raises(ValueError, match="positive"):
         TokenBudgetScheduler(max_num_seqs=0)
+
+
+def test_synthetic_config_validation_needs_no_gpu():
+    from inferkernellab_b200.decode import SyntheticDecoderConfig
+
+    with pytest.raises(ValueError, match="unsupported attention backend"):
+        SyntheticDecoderConfig(backend="paged_reference")
+    with pytest.raises(ValueError, match="unsupported append backend"):
+        SyntheticDecoderConfig(append_backend="torch")
+    with pytest.raises(ValueError, match="divisible"):
+        SyntheticDecoderConfig(num_heads=6, num_kv_heads=4)
+    with pytest.raises(ValueError, match="CUDA device"):
+        SyntheticDecoderConfig(device="cpu")
+    with pytest.raises(ValueError, match="float16 or bfloat16"):
+        SyntheticDecoderConfig(dtype=torch.float32)
+
+
+def test_llama_runner_validation_needs_no_gpu():
+    pytest.importorskip("transformers")
+    from inferkernellab_b200.llama import LlamaPagedDecodeRunner, load_random_llama
+
+    model = load_random_llama(vocab_size=32, hidden_size=32, intermediate_size=64, num_layers=1,
+                              num_attention_heads=2, num_kv_heads=1, max_position_embeddings=32,
+                              rope_theta=10_000.0, seed=1, device="cpu", dtype=torch.float32)
+    with pytest.raises(ValueError, match="unsupported backend"):
+        LlamaPagedDecodeRunner(model, [[1, 2]], max_new_tokens=1, backend="triton_paged")
+    with pytest.raises(ValueError, match="CUDA device"):
+        LlamaPagedDecodeRunner(model, [[1, 2]], max_new_tokens=1)
+    with pytest.raises(ValueError, match="top_p"):
+        LlamaPagedDecodeRunner(model, [[1, 2]], max_new_tokens=1, top_p=0.0)
