@@ -14,7 +14,11 @@ on the sm_100a kernels:
   ``build_slot_mapping`` launch per batch, K/V go in with ``append_kv`` and the
   causal attention runs in ``paged_prefill_attention_varlen``;
 * decode appends each request's new K/V and runs ``paged_decode_attention``;
-  the step's slots and lengths are built once and reused by all layers.
+  the step's slots and lengths are built once and reused by all layers;
+* ``cuda_graph=True`` captures the whole decode step (every layer, lm_head)
+  into one CUDA graph with device-resident metadata and replays it each step,
+  instead of re-launching ~35 kernels per layer from Python every step as the
+  reference runner does.
 
 Multi-GPU: requests are partitioned over ranks by the caller; each rank runs its
 own runner (own block pool) and passes ``token_exchange`` -- e.g.
@@ -107,7 +111,8 @@ class LlamaPagedDecodeRunner:
                  max_num_batched_tokens: int = 2048, prefill_mode: str = "batched",
                  temperature: float = 0.0, top_p: float = 1.0, seed: int = 2026,
                  eos_token_ids: Sequence[int] | None = None,
-                 token_exchange: TokenExchange | None = None, collect_logits: bool = True):
+                 token_exchange: TokenExchange | None = None, collect_logits: bool = True,
+                 cuda_graph: bool = False):
         if not prompts:
             raise ValueError("at least one prompt is required")
         if max_new_tokens <= 0:
@@ -142,6 +147,8 @@ class LlamaPagedDecodeRunner:
             raise ValueError("EOS token id is outside the configured vocabulary")
         self.token_exchange = token_exchange
         self.collect_logits = collect_logits
+        self.cuda_graph = cuda_graph
+        self._graph: _DecodeGraph | None = None
         self.prompt_lengths = tuple(len(p) for p in self.prompts)
         cfg = model.config
         self.num_layers = int(cfg.num_hidden_layers)
@@ -209,24 +216,29 @@ class LlamaPagedDecodeRunner:
             hidden = self._layer_tail(layer, residual, attended, n)
         return self.model.model.norm(hidden)
 
-    def _forward_decode(self, token_ids, requests, positions: Sequence[int]) -> torch.Tensor:
-        self.meta.sync(requests)
+    def _decode_body(self, token_ids: torch.Tensor, positions: torch.Tensor,
+                     tables: torch.Tensor) -> torch.Tensor:
+        """One decode step from device tensors only (capturable in a CUDA graph).
+
+        ``positions`` int32 ``[B]``: where each request's new token goes; the
+        step appends its K/V there and attends over ``positions + 1`` tokens."""
         bs, nb = self.cache.layout.block_size, self.cache.layout.num_blocks
-        starts = torch.tensor([list(positions), [p + 1 for p in positions]], dtype=torch.int32)
-        starts = starts.to(self.device, non_blocking=True)
-        tables = self.meta.rows(requests)
-        slots, _ = build_slot_mapping(tables, starts[0], starts[1], block_size=bs, num_blocks=nb,
-                                      total_tokens=len(positions), with_cu_seqlens=False)
-        lens = starts[1]
-        pos = starts[0].to(torch.long)
+        lens = positions + 1
+        slots, _ = build_slot_mapping(tables, positions, lens, block_size=bs, num_blocks=nb,
+                                      total_tokens=positions.shape[0], with_cu_seqlens=False)
 
         def attend(layer, q, k, v):
             append_kv(k, v, self.cache, slots, layer=layer)
             return paged_decode_attention(q, self.cache, tables, lens, layer=layer,
                                           validate_inputs=False)
 
-        hidden = self._forward(token_ids, pos, attend)
+        hidden = self._forward(token_ids, positions.to(torch.long), attend)
         return self.model.lm_head(hidden)
+
+    def _forward_decode(self, token_ids, requests, positions: Sequence[int]) -> torch.Tensor:
+        self.meta.sync(requests)
+        pos = torch.tensor(list(positions), dtype=torch.int32).to(self.device, non_blocking=True)
+        return self._decode_body(token_ids, pos, self.meta.rows(requests))
 
     def _forward_prefill_packed(self, requests, starts, ends) -> torch.Tensor:
         """Packed ranges of one budget batch; returns hidden of every token ``[sum T, H]``."""
@@ -310,7 +322,14 @@ class LlamaPagedDecodeRunner:
         if self.token_exchange is not None:
             self.token_exchange(next_tokens)
         positions = [r.prompt_tokens + r.generated_tokens for r in requests]
-        next_logits = self._forward_decode(next_tokens, requests, positions)
+        ids = [r.request_id for r in requests]
+        if self.cuda_graph and ids == list(range(len(ids))):
+            if self._graph is None or self._graph.batch != len(ids):
+                self._graph = _DecodeGraph(self, requests, next_tokens, positions)
+            self.meta.sync(requests)
+            next_logits = self._graph.replay(next_tokens, positions)
+        else:
+            next_logits = self._forward_decode(next_tokens, requests, positions)
         if self.collect_logits:
             self._decode_logits.append(used.detach().float().cpu())
         tokens = next_tokens.tolist()
@@ -379,6 +398,46 @@ class LlamaPagedDecodeRunner:
             peak_memory_allocated_bytes=int(torch.cuda.max_memory_allocated(self.device)),
             peak_kv_memory_bytes=peak_kv, used_blocks_peak=used_peak,
             cache_released=cache_released and self.cache.allocator.num_used_blocks == 0)
+
+
+class _DecodeGraph:
+    """The whole decode step of a fixed batch (all layers + lm_head) as one CUDA graph.
+
+    Inputs live in static device buffers: the token ids and positions are
+    copied in before each replay, the block tables are the runner's persistent
+    device table rows (grown in place by ``DeviceBlockTables.sync``).  The
+    slots and lengths are derived on the device inside the graph.  Capture
+    runs on a side stream after one eager warm-up step that sets up the
+    kernels' workspaces, as CUDA graph capture requires.
+    """
+
+    def __init__(self, runner: "LlamaPagedDecodeRunner", requests, tokens: torch.Tensor,
+                 positions: Sequence[int]):
+        self.batch = len(requests)
+        device = runner.device
+        runner.meta.sync(requests)
+        self.tables = runner.meta.rows(requests)
+        self.tokens = tokens.detach().clone().to(torch.long)
+        self.positions = torch.tensor(list(positions), dtype=torch.int32, device=device)
+        self._host_pos = torch.empty(self.batch, dtype=torch.int32, pin_memory=True)
+        stream = torch.cuda.Stream(device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(stream):
+            # Warm-up (eager) on the capture stream; it writes the same K/V the
+            # replay below rewrites, so it has no effect on results.
+            runner._decode_body(self.tokens, self.positions, self.tables)
+        stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self.logits = runner._decode_body(self.tokens, self.positions, self.tables)
+        torch.cuda.current_stream(device).wait_stream(stream)
+
+    def replay(self, tokens: torch.Tensor, positions: Sequence[int]) -> torch.Tensor:
+        self._host_pos.copy_(torch.tensor(list(positions), dtype=torch.int32))
+        self.positions.copy_(self._host_pos, non_blocking=True)
+        self.tokens.copy_(tokens)
+        self.graph.replay()
+        return self.logits
 
 
 # ------------------------------------------------------------------ helpers

@@ -89,3 +89,16 @@ def test_llama_sampling_is_seeded():
                                top_p=0.9, seed=7).run()
     assert a.generated_tokens == b.generated_tokens
     assert all(len(x) == 4 for x in a.token_logprobs)
+
+
+def test_llama_cuda_graph_decode_matches_eager_decode():
+    model = _model(torch.bfloat16, num_kv_heads=2, num_layers=2, hidden=256, heads=2)
+    prompts = tuple(tuple((5 * i + j) % 128 for j in range(n)) for i, n in enumerate([40, 7, 33]))
+    eager = LlamaPagedDecodeRunner(model, prompts, max_new_tokens=20, block_size=16).run()
+    graph = LlamaPagedDecodeRunner(model, prompts, max_new_tokens=20, block_size=16,
+                                   cuda_graph=True).run()
+    assert graph.generated_tokens == eager.generated_tokens
+    for a, b in zip(graph.decode_logits, eager.decode_logits):
+        assert torch.allclose(a, b, atol=1e-3, rtol=0)
+    assert graph.cache_released
+    _assert_ok(correctness(model, prompts, graph))
