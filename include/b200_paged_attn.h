@@ -157,6 +157,35 @@ B200_API int b200_append_kv(const b200_cache_desc* cache, int32_t layer, const v
                    int64_t value_stride_token, int64_t value_stride_head, const void* slots,
                    int32_t slots_dtype, uint32_t* error_word, void* stream);
 
+/* ------------------------------------------------- fused rotary + append
+ * For every token t and head h (rotate_half(x) = concat(-x[D/2:], x[:D/2])):
+ *   query_out[t, h]            = query[t, h] * cos[t] + rotate_half(query[t, h]) * sin[t]
+ *   cache.K[layer, slot[t], h] = key[t, h]   * cos[t] + rotate_half(key[t, h])   * sin[t]
+ *   cache.V[layer, slot[t], h] = value[t, h]
+ * rounded to the 16-bit type after each multiply and after the add, exactly like
+ * the reference's torch elementwise rotary (reference hf_benchmark.py:69-85), so
+ * results are bit-identical to rotating with torch and then calling
+ * b200_append_kv.  One launch replaces the rotary ops, the layout copies and the
+ * append of a layer (decode step or packed prefill batch).  cos/sin: [T, D] in
+ * the cache dtype.  Slot rules as b200_append_kv.
+ */
+typedef struct {
+  int64_t num_tokens;
+  int32_t num_q_heads;
+  int32_t layer;
+  int64_t q_stride_token, q_stride_head; /* elements */
+  int64_t k_stride_token, k_stride_head;
+  int64_t v_stride_token, v_stride_head;
+  int64_t q_out_stride_token, q_out_stride_head;
+  int64_t cos_stride_token, sin_stride_token;
+  int32_t slots_dtype; /* B200_I32 / B200_I64 */
+} b200_rope_append_args;
+
+B200_API int b200_rope_append_kv(const b200_cache_desc* cache, const b200_rope_append_args* args,
+                                 const void* query, const void* key, const void* value,
+                                 const void* cos, const void* sin, const void* slots,
+                                 void* query_out, uint32_t* error_word, void* stream);
+
 /* ----------------------------------------------------------------- prefill
  * Ragged causal prefill attention over the paged cache.  Sequence b owns the
  * query tokens of logical positions query_starts[b] .. context_lens[b]-1; a

@@ -5,6 +5,7 @@ operators plus host mirrors of its cache, scheduler and runtime:
 
 * ``paged_decode_attention`` -- split-KV paged decode (MHA/GQA/MQA);
 * ``append_kv`` -- reshape-and-cache through ``slot_mapping``, bit-exact;
+* ``rope_append_kv`` -- rotary embedding of q/k fused with the K/V append;
 * ``paged_prefill_attention`` / ``paged_prefill_attention_varlen`` -- ragged
   causal prefill over the paged cache;
 * ``build_slot_mapping`` -- device-built slots + ``cu_seqlens`` for a batch;
@@ -26,6 +27,7 @@ from .ops import (
     paged_decode_attention,
     paged_prefill_attention,
     paged_prefill_attention_varlen,
+    rope_append_kv,
 )
 from .runtime import InferenceRuntime, RuntimeStats
 from .scheduler import InferenceRequest, ScheduleBatch, TokenBudgetScheduler
@@ -59,4 +61,5 @@ __all__ = [
     "paged_prefill_attention",
     "paged_prefill_attention_b200",
     "paged_prefill_attention_varlen",
+    "rope_append_kv",
 ]

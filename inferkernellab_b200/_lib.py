@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "b200_paged_decode_noalloc",
     "b200_paged_decode_noalloc_scratch_bytes",
     "b200_append_kv",
+    "b200_rope_append_kv",
     "b200_paged_prefill",
     "b200_build_slot_mapping",
     "b200_validate_decode_metadata",
@@ -101,6 +102,25 @@ class PrefillArgs(ctypes.Structure):
     ]
 
 
+class RopeAppendArgs(ctypes.Structure):
+    _fields_ = [
+        ("num_tokens", ctypes.c_int64),
+        ("num_q_heads", ctypes.c_int32),
+        ("layer", ctypes.c_int32),
+        ("q_stride_token", ctypes.c_int64),
+        ("q_stride_head", ctypes.c_int64),
+        ("k_stride_token", ctypes.c_int64),
+        ("k_stride_head", ctypes.c_int64),
+        ("v_stride_token", ctypes.c_int64),
+        ("v_stride_head", ctypes.c_int64),
+        ("q_out_stride_token", ctypes.c_int64),
+        ("q_out_stride_head", ctypes.c_int64),
+        ("cos_stride_token", ctypes.c_int64),
+        ("sin_stride_token", ctypes.c_int64),
+        ("slots_dtype", ctypes.c_int32),
+    ]
+
+
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
@@ -115,6 +135,9 @@ _PROTOTYPES = {
     "b200_paged_decode_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "b200_append_kv": (ctypes.c_int, [ctypes.POINTER(CacheDesc), _i32, _vp, _vp, _i64, _i64, _i64,
                                       _i64, _i64, _vp, _i32, _vp, _vp]),
+    "b200_rope_append_kv": (ctypes.c_int, [ctypes.POINTER(CacheDesc),
+                                           ctypes.POINTER(RopeAppendArgs), _vp, _vp, _vp, _vp,
+                                           _vp, _vp, _vp, _vp, _vp]),
     "b200_paged_prefill": (ctypes.c_int, [ctypes.POINTER(CacheDesc), ctypes.POINTER(PrefillArgs),
                                           _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_build_slot_mapping": (ctypes.c_int, [_vp, _i32, _i64, _i32, _vp, _vp, _i32, _i32, _i32,

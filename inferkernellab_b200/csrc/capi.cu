@@ -12,6 +12,7 @@
 #include "host_common.h"
 #include "metadata.h"
 #include "prefill.h"
+#include "rope_append.h"
 
 namespace b200 {
 const char* last_error_cstr();
@@ -74,6 +75,16 @@ int b200_append_kv(const b200_cache_desc* cache, int32_t layer, const void* key,
     return b200::launch_append_kv(cache, layer, key, value, num_tokens, key_stride_token,
                                   key_stride_head, value_stride_token, value_stride_head, slots,
                                   slots_dtype, error_word, as_stream(stream));
+  });
+}
+
+int b200_rope_append_kv(const b200_cache_desc* cache, const b200_rope_append_args* args,
+                        const void* query, const void* key, const void* value, const void* cos,
+                        const void* sin, const void* slots, void* query_out,
+                        uint32_t* error_word, void* stream) {
+  return guarded([&] {
+    return b200::launch_rope_append(cache, args, query, key, value, cos, sin, slots, query_out,
+                                    error_word, as_stream(stream));
   });
 }
 

@@ -1,0 +1,178 @@
+// Fused rotary embedding + KV append for sm_100a.
+//
+// For every token t (a decode step's new tokens or a prefill batch's packed
+// tokens) and head h:
+//   q_out[t, h]                    = rope(q[t, h], cos[t], sin[t])
+//   cache.K[layer, slot[t], h]     = rope(k[t, h], cos[t], sin[t])
+//   cache.V[layer, slot[t], h]     = v[t, h]
+// with rope(x)[i] = x[i] * cos[i] + rotate_half(x)[i] * sin[i],
+// rotate_half(x) = concat(-x[D/2:], x[:D/2]) -- the rotation the reference
+// applies with torch elementwise ops (hf_benchmark.py:69-85).  Each of those ops
+// rounds to the 16-bit type, so the kernel rounds at the same three points
+// (x*cos, rotate_half(x)*sin, their sum): its output is bit-identical to the
+// reference's, and the appended K/V equal what append_kv would store.
+// One launch replaces the rotary ops, the layout copies and the append.
+#include "../../include/b200_paged_attn.h"
+#include "common.cuh"
+#include "host_common.h"
+#include "rope_append.h"
+
+namespace b200 {
+
+struct RopeParams {
+  const uint8_t* q;
+  const uint8_t* k;
+  const uint8_t* v;
+  const uint8_t* cos;
+  const uint8_t* sin;
+  uint8_t* q_out;
+  uint8_t* k_cache;
+  uint8_t* v_cache;
+  const void* slots;
+  uint32_t* err;
+  long long num_tokens;
+  long long q_st, q_sh, k_st, k_sh, v_st, v_sh;  // strides, elements
+  long long qo_st, qo_sh;
+  long long cos_st, sin_st;
+  long long num_slots, layer_slot_base;
+  int num_q_heads, num_kv_heads, head_dim, slots64;
+};
+
+template <typename E>
+__device__ __forceinline__ float to_f(typename E::T x);
+template <>
+__device__ __forceinline__ float to_f<Half>(__half x) {
+  return __half2float(x);
+}
+template <>
+__device__ __forceinline__ float to_f<BF16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+// Round-trip through the 16-bit type (what one torch elementwise op does).
+template <typename E>
+__device__ __forceinline__ float rnd(float x) {
+  return to_f<E>(from_float<E>(x));
+}
+
+template <typename E>
+__global__ void __launch_bounds__(256) rope_append_kernel(const RopeParams p) {
+  using T = typename E::T;
+  const int half = p.head_dim / 2;
+  // Work items per token: rotated rows (q heads, then k heads) x half-pairs,
+  // then V rows x half-pairs (two elements copied per item).
+  const int rot_rows = p.num_q_heads + p.num_kv_heads;
+  const long long per_token = static_cast<long long>(rot_rows + p.num_kv_heads) * half;
+  const long long total = p.num_tokens * per_token;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long t = idx / per_token;
+    const int rem = static_cast<int>(idx - t * per_token);
+    const int row = rem / half;
+    const int i = rem - row * half;
+    const bool is_q = row < p.num_q_heads;
+    const bool is_k = !is_q && row < rot_rows;
+    long long slot = 0;
+    if (!is_q) {
+      slot = load_index(p.slots, t, p.slots64);
+      if (slot < 0) continue;  // padding slot: nothing to append
+      if (slot >= p.num_slots) {
+        if (p.err) atomicOr(p.err, kErrBadSlot);
+        continue;
+      }
+    }
+    if (is_q || is_k) {
+      const T* src;
+      if (is_q)
+        src = reinterpret_cast<const T*>(p.q) + t * p.q_st + row * p.q_sh;
+      else
+        src = reinterpret_cast<const T*>(p.k) + t * p.k_st + (row - p.num_q_heads) * p.k_sh;
+      const T* c = reinterpret_cast<const T*>(p.cos) + t * p.cos_st;
+      const T* s = reinterpret_cast<const T*>(p.sin) + t * p.sin_st;
+      const float x1 = to_f<E>(src[i]);
+      const float x2 = to_f<E>(src[i + half]);
+      // first half: x1*cos - x2*sin ; second half: x2*cos + x1*sin (rounded like torch)
+      const float lo = rnd<E>(rnd<E>(x1 * to_f<E>(c[i])) + rnd<E>(-x2 * to_f<E>(s[i])));
+      const float hi =
+          rnd<E>(rnd<E>(x2 * to_f<E>(c[i + half])) + rnd<E>(x1 * to_f<E>(s[i + half])));
+      T* dst;
+      if (is_q) {
+        dst = reinterpret_cast<T*>(p.q_out) + t * p.qo_st + row * p.qo_sh;
+      } else {
+        const int h = row - p.num_q_heads;
+        dst = reinterpret_cast<T*>(p.k_cache) +
+              ((p.layer_slot_base + slot) * p.num_kv_heads + h) * p.head_dim;
+      }
+      dst[i] = from_float<E>(lo);
+      dst[i + half] = from_float<E>(hi);
+    } else {
+      const int h = row - rot_rows;
+      const T* src = reinterpret_cast<const T*>(p.v) + t * p.v_st + h * p.v_sh;
+      T* dst = reinterpret_cast<T*>(p.v_cache) +
+               ((p.layer_slot_base + slot) * p.num_kv_heads + h) * p.head_dim;
+      dst[i] = src[i];
+      dst[i + half] = src[i + half];
+    }
+  }
+}
+
+int launch_rope_append(const b200_cache_desc* c, const b200_rope_append_args* a, const void* query,
+                       const void* key, const void* value, const void* cos, const void* sin,
+                       const void* slots, void* query_out, uint32_t* error_word,
+                       cudaStream_t stream) {
+  if (c == nullptr || a == nullptr) return set_error(B200_ERR_INVALID, "null descriptor");
+  if (c->num_layers <= 0 || c->num_blocks <= 0 || c->block_size <= 0 || c->num_kv_heads <= 0 ||
+      c->head_dim <= 0)
+    return set_error(B200_ERR_INVALID, "cache dimensions must be positive");
+  if (c->dtype != B200_F16 && c->dtype != B200_BF16)
+    return set_error(B200_ERR_UNSUPPORTED, "cache dtype must be float16 or bfloat16");
+  if (c->head_dim % 2 != 0) return set_error(B200_ERR_INVALID, "head_dim must be even for rotary");
+  if (a->layer < 0 || a->layer >= c->num_layers)
+    return set_error(B200_ERR_LAYER, "layer is out of range");
+  if (a->num_q_heads <= 0 || a->num_q_heads % c->num_kv_heads != 0)
+    return set_error(B200_ERR_INVALID, "num_heads must be divisible by num_kv_heads");
+  if (a->num_tokens < 0) return set_error(B200_ERR_INVALID, "num_tokens must be non-negative");
+  if (a->num_tokens == 0) return B200_OK;
+  if (!query || !key || !value || !cos || !sin || !slots || !query_out || !c->k_cache ||
+      !c->v_cache)
+    return set_error(B200_ERR_INVALID, "null tensor pointer");
+  RopeParams p;
+  p.q = static_cast<const uint8_t*>(query);
+  p.k = static_cast<const uint8_t*>(key);
+  p.v = static_cast<const uint8_t*>(value);
+  p.cos = static_cast<const uint8_t*>(cos);
+  p.sin = static_cast<const uint8_t*>(sin);
+  p.q_out = static_cast<uint8_t*>(query_out);
+  p.k_cache = static_cast<uint8_t*>(c->k_cache);
+  p.v_cache = static_cast<uint8_t*>(c->v_cache);
+  p.slots = slots;
+  p.err = error_word;
+  p.num_tokens = a->num_tokens;
+  p.q_st = a->q_stride_token;
+  p.q_sh = a->q_stride_head;
+  p.k_st = a->k_stride_token;
+  p.k_sh = a->k_stride_head;
+  p.v_st = a->v_stride_token;
+  p.v_sh = a->v_stride_head;
+  p.qo_st = a->q_out_stride_token;
+  p.qo_sh = a->q_out_stride_head;
+  p.cos_st = a->cos_stride_token;
+  p.sin_st = a->sin_stride_token;
+  p.num_slots = static_cast<long long>(c->num_blocks) * c->block_size;
+  p.layer_slot_base = static_cast<long long>(a->layer) * p.num_slots;
+  p.num_q_heads = a->num_q_heads;
+  p.num_kv_heads = c->num_kv_heads;
+  p.head_dim = c->head_dim;
+  p.slots64 = a->slots_dtype == B200_I64;
+  const long long work =
+      a->num_tokens * (a->num_q_heads + 2LL * c->num_kv_heads) * (c->head_dim / 2);
+  long long blocks = (work + 255) / 256;
+  if (blocks > 148LL * 32) blocks = 148LL * 32;
+  if (c->dtype == B200_BF16)
+    rope_append_kernel<BF16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
+  else
+    rope_append_kernel<Half><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
+  return cuda_status(cudaGetLastError(), "rope_append_kernel launch");
+}
+
+}  // namespace b200

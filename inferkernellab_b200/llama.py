@@ -11,10 +11,14 @@ on the sm_100a kernels:
 * batched prefill is *packed*: the scheduled ranges of a budget batch are
   concatenated (no padding rows, unlike the reference's ``_prefill_batch``
   ``:522-547``), slots and ``cu_seqlens`` come from one device
-  ``build_slot_mapping`` launch per batch, K/V go in with ``append_kv`` and the
-  causal attention runs in ``paged_prefill_attention_varlen``;
-* decode appends each request's new K/V and runs ``paged_decode_attention``;
-  the step's slots and lengths are built once and reused by all layers;
+  ``build_slot_mapping`` launch per batch and the causal attention runs in
+  ``paged_prefill_attention_varlen``;
+* decode runs ``paged_decode_attention``; the step's slots and lengths are
+  built once and reused by all layers;
+* in both, one ``rope_append_kv`` launch per layer applies the rotary embedding
+  to q and k (bit-identical to the reference's ``_apply_rotary``) and writes
+  the rotated K and V into the cache, in place of the reference's separate
+  rotary ops, layout copies and append;
 * ``cuda_graph=True`` captures the whole decode step (every layer, lm_head)
   into one CUDA graph with device-resident metadata and replays it each step,
   instead of re-launching ~35 kernels per layer from Python every step as the
@@ -38,23 +42,14 @@ import torch
 
 from .cache import PagedKVCache
 from .decode import DeviceBlockTables, _percentile
-from .ops import append_kv, build_slot_mapping, paged_decode_attention, paged_prefill_attention_varlen
+from .ops import (
+    build_slot_mapping,
+    paged_decode_attention,
+    paged_prefill_attention_varlen,
+    rope_append_kv,
+)
 from .runtime import InferenceRuntime
 from .scheduler import InferenceRequest, TokenBudgetScheduler
-
-
-def _rotate_half(x: torch.Tensor) -> torch.Tensor:
-    first, second = x[..., : x.shape[-1] // 2], x[..., x.shape[-1] // 2:]
-    return torch.cat((-second, first), dim=-1)
-
-
-def _apply_rotary(query, key, cos, sin):
-    """Rotary embedding as the reference applies it (hf_benchmark.py:69-85).
-
-    ``query``/``key`` ``[..., heads, D]``; ``cos``/``sin`` broadcast over heads."""
-    cos = cos.unsqueeze(-2)
-    sin = sin.unsqueeze(-2)
-    return query * cos + _rotate_half(query) * sin, key * cos + _rotate_half(key) * sin
 
 
 @dataclass(frozen=True)
@@ -186,13 +181,12 @@ class LlamaPagedDecodeRunner:
         self._has_run = False
 
     # ------------------------------------------------------------------ layers
-    def _layer_qkv(self, layer, hidden, cos, sin, tokens: int):
+    def _layer_qkv(self, layer, hidden, tokens: int):
         attn = layer.self_attn
         q = attn.q_proj(hidden).view(tokens, self.num_heads, self.head_dim)
         k = attn.k_proj(hidden).view(tokens, self.num_kv_heads, self.head_dim)
         v = attn.v_proj(hidden).view(tokens, self.num_kv_heads, self.head_dim)
-        q, k = _apply_rotary(q, k, cos, sin)
-        return q.contiguous(), k.contiguous(), v.contiguous()
+        return q, k, v
 
     def _layer_tail(self, layer, residual, attended, tokens: int):
         hidden = residual + layer.self_attn.o_proj(attended.reshape(tokens, -1))
@@ -202,8 +196,12 @@ class LlamaPagedDecodeRunner:
                                      * layer.mlp.up_proj(hidden))
         return residual + hidden
 
-    def _forward(self, token_ids: torch.Tensor, positions: torch.Tensor, attend) -> torch.Tensor:
-        """Shared layer loop on a flat token batch ``[N]``; returns hidden ``[N, H]``."""
+    def _forward(self, token_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
+                 attend) -> torch.Tensor:
+        """Shared layer loop on a flat token batch ``[N]``; returns hidden ``[N, H]``.
+
+        Per layer: projections, then one ``rope_append_kv`` (rotary on q/k and
+        K/V into ``slots``), then ``attend(layer, rotated_q)``."""
         n = token_ids.shape[0]
         hidden = self.model.model.embed_tokens(token_ids.to(torch.long))
         cos, sin = self.model.model.rotary_emb(hidden.unsqueeze(0), positions.view(1, -1))
@@ -211,8 +209,9 @@ class LlamaPagedDecodeRunner:
         for index, layer in enumerate(self.model.model.layers):
             residual = hidden
             hidden = layer.input_layernorm(hidden)
-            q, k, v = self._layer_qkv(layer, hidden, cos, sin, n)
-            attended = attend(index, q, k, v)
+            q, k, v = self._layer_qkv(layer, hidden, n)
+            q = rope_append_kv(q, k, v, cos, sin, self.cache, slots, layer=index)
+            attended = attend(index, q)
             hidden = self._layer_tail(layer, residual, attended, n)
         return self.model.model.norm(hidden)
 
@@ -227,12 +226,11 @@ class LlamaPagedDecodeRunner:
         slots, _ = build_slot_mapping(tables, positions, lens, block_size=bs, num_blocks=nb,
                                       total_tokens=positions.shape[0], with_cu_seqlens=False)
 
-        def attend(layer, q, k, v):
-            append_kv(k, v, self.cache, slots, layer=layer)
+        def attend(layer, q):
             return paged_decode_attention(q, self.cache, tables, lens, layer=layer,
                                           validate_inputs=False)
 
-        hidden = self._forward(token_ids, positions.to(torch.long), attend)
+        hidden = self._forward(token_ids, positions.to(torch.long), slots, attend)
         return self.model.lm_head(hidden)
 
     def _forward_decode(self, token_ids, requests, positions: Sequence[int]) -> torch.Tensor:
@@ -257,12 +255,11 @@ class LlamaPagedDecodeRunner:
         ids = ids.to(self.device, non_blocking=True)
         pos = pos.to(self.device, non_blocking=True)
 
-        def attend(layer, q, k, v):
-            append_kv(k, v, self.cache, slots, layer=layer)
+        def attend(layer, q):
             return paged_prefill_attention_varlen(q, self.cache, tables, cu, meta[0], meta[1],
                                                   layer=layer)
 
-        return self._forward(ids, pos, attend)
+        return self._forward(ids, pos, slots, attend)
 
     # ------------------------------------------------------------------- hooks
     def _prefill(self, request: InferenceRequest, start: int, end: int) -> None:

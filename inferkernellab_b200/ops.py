@@ -292,6 +292,71 @@ def append_kv(key: torch.Tensor, value: torch.Tensor, cache, slots: torch.Tensor
         _stream_ptr(key.device)))
 
 
+def rope_append_kv(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                   cos: torch.Tensor, sin: torch.Tensor, cache, slots: torch.Tensor,
+                   layer: int = 0, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Rotate ``query``/``key`` and append rotated K and V to ``cache`` in one launch.
+
+    ``query`` ``[T, Hq, D]``, ``key``/``value`` ``[T, Hkv, D]``, ``cos``/``sin``
+    ``[T, D]`` (the per-token rows of the model's rotary table, cache dtype).
+    Returns the rotated query (written to ``out`` when given).  Bit-identical to
+    the reference's ``_apply_rotary`` (``hf_benchmark.py:69-85``: rounded torch
+    elementwise ``x * cos + rotate_half(x) * sin``) followed by
+    ``append_kv_triton(key, value, cache, slots, layer)`` (``append.py:69-106``).
+    ``query``/``key``/``value`` may be strided views (for instance slices of one
+    fused QKV projection) as long as their last dimension is contiguous.
+    """
+    if query.ndim != 3 or key.ndim != 3 or value.shape != key.shape:
+        raise ValueError("query must be [T, Hq, D] and key/value [T, Hkv, D]")
+    device = query.device
+    if device.type != "cuda" or any(t.device != device for t in (key, value, cos, sin, slots)):
+        raise ValueError("query/key/value/cos/sin/slots must be on the same CUDA device")
+    layout = cache.layout
+    tokens, heads, dim = query.shape
+    if tuple(key.shape) != (tokens, layout.num_kv_heads, layout.head_dim) or dim != layout.head_dim:
+        raise ValueError("query/key/value shape does not match cache layout")
+    if heads % layout.num_kv_heads != 0:
+        raise ValueError("num_heads must be divisible by num_kv_heads")
+    if dim % 2:
+        raise ValueError("head_dim must be even for rotary embeddings")
+    cos = cos.reshape(-1, dim)
+    sin = sin.reshape(-1, dim)
+    if cos.shape[0] != tokens or sin.shape[0] != tokens:
+        raise ValueError("cos/sin must hold one [D] row per token")
+    if slots.numel() != tokens:
+        raise ValueError("slots and query token counts must match")
+    if not 0 <= layer < layout.num_layers:
+        raise IndexError("layer is out of range")
+    dtype = cache.k.dtype
+    if any(t.dtype != dtype for t in (query, key, value, cos, sin)):
+        raise ValueError("query/key/value/cos/sin must have the cache dtype")
+    if slots.dtype not in _INDEX_CODE:
+        raise ValueError("slots must use int32 or int64")
+    if out is None:
+        out = torch.empty((tokens, heads, dim), dtype=dtype, device=device)
+    elif out.shape != query.shape or out.dtype != dtype or out.device != device:
+        raise ValueError("out must match query's shape, dtype and device")
+    if tokens == 0:
+        return out
+    query, key, value, out = (t if t.stride(-1) == 1 else t.contiguous()
+                              for t in (query, key, value, out))
+    cos = cos if cos.stride(-1) == 1 else cos.contiguous()
+    sin = sin if sin.stride(-1) == 1 else sin.contiguous()
+    slots = slots.reshape(-1)
+    if not slots.is_contiguous():
+        slots = slots.contiguous()
+    args = _lib.RopeAppendArgs(tokens, heads, layer, query.stride(0), query.stride(1),
+                               key.stride(0), key.stride(1), value.stride(0), value.stride(1),
+                               out.stride(0), out.stride(1), cos.stride(0), sin.stride(0),
+                               _INDEX_CODE[slots.dtype])
+    desc = _cache_desc(cache)
+    _lib.check(_lib.load().b200_rope_append_kv(
+        ctypes.byref(desc), ctypes.byref(args), query.data_ptr(), key.data_ptr(),
+        value.data_ptr(), cos.data_ptr(), sin.data_ptr(), slots.data_ptr(), out.data_ptr(),
+        _ERROR_WORDS.get(device).data_ptr(), _stream_ptr(device)))
+    return out
+
+
 # ------------------------------------------------------------------- prefill
 
 def _prefill_index(values, device) -> tuple[torch.Tensor, list[int]]:

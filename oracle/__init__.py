@@ -1,8 +1,9 @@
 """CPU oracle for the paged-KV attention path.  TEST INFRASTRUCTURE ONLY.
 
 This package is a numpy restatement of InferKernelLab's reference algorithms for
-the paged KV cache and paged attention (``src/inferkernellab/cache.py`` and
-``src/inferkernellab/attention.py`` in the reference project).  It is the checker
+the paged KV cache and paged attention (``src/inferkernellab/cache.py``,
+``src/inferkernellab/attention.py`` and the rotary helpers of
+``src/inferkernellab/hf_benchmark.py`` in the reference project).  It is the checker
 that the CUDA path is compared against, never a code path of the product:
 
 * only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` /
@@ -21,6 +22,7 @@ from .paged_ref import (  # noqa: F401
     to_f32,
     slot_mapping,
     write_slots,
+    rotary_embed,
     read_tokens,
     dense_decode_attention,
     paged_decode_attention,

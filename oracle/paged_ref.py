@@ -97,6 +97,38 @@ def write_slots(k_store: np.ndarray, v_store: np.ndarray, layer: int, slots, key
     v_store[layer, blocks, offsets] = value
 
 
+def _round_to(values: np.ndarray, kind: str) -> np.ndarray:
+    """Round float32 to ``kind`` and widen back (what one torch elementwise op stores)."""
+    if kind == "bf16":
+        return bf16_bits_to_f32(f32_to_bf16_bits(values))
+    if kind == "f16":
+        return np.asarray(values, dtype=np.float32).astype(np.float16).astype(np.float32)
+    return np.asarray(values, dtype=np.float32)
+
+
+def rotary_embed(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, kind: str) -> np.ndarray:
+    """Rotary embedding of ``x`` ``[T, H, D]`` with per-token ``cos``/``sin`` ``[T, D]``.
+
+    Follows ``_rotate_half`` / ``_apply_rotary`` (reference
+    ``hf_benchmark.py:69-85``): ``x * cos + rotate_half(x) * sin`` with
+    ``rotate_half(x) = concat(-x[D/2:], x[:D/2])``, evaluated as torch does for a
+    16-bit dtype -- each product and the sum computed in float32 and rounded to
+    ``kind``.  Inputs and output are stored arrays of element kind ``kind``
+    (bfloat16 as raw uint16 bits).
+    """
+    xf = to_f32(x, kind)
+    cf = to_f32(cos, kind)[:, None, :]
+    sf = to_f32(sin, kind)[:, None, :]
+    half = xf.shape[-1] // 2
+    rot = np.concatenate((-xf[..., half:], xf[..., :half]), axis=-1)
+    out = _round_to(_round_to(xf * cf, kind) + _round_to(rot * sf, kind), kind)
+    if kind == "bf16":
+        return f32_to_bf16_bits(out)
+    if kind == "f16":
+        return out.astype(np.float16)
+    return out
+
+
 def read_tokens(store: np.ndarray, layer: int, block_table, length: int) -> np.ndarray:
     """First ``length`` logical tokens of one request, in order (reference ``cache.py:191-200``)."""
     _, num_blocks, block_size, _, _ = store.shape

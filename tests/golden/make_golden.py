@@ -13,6 +13,8 @@ torch, CPU) and records, for seeded inputs, what the reference computes:
                             form) and on the native-dtype cache;
 * ``prefill_*.npz``      -- ``paged_prefill_attention_sdpa`` (``attention.py:230-321``);
 * ``append.npz``         -- ``PagedKVCache.write_slots`` (``cache.py:156-189``);
+* ``rotary.npz``         -- ``_apply_rotary`` (``hf_benchmark.py:69-85``) in fp16
+                            and bf16, with cos/sin from a Llama rotary table;
 * ``runtime_events.json``-- ``InferenceRuntime`` hook traces (``runtime.py:65-104``)
                             and ``TokenBudgetScheduler`` packing (``scheduler.py:50-84``);
 * ``synthetic_decoder.json`` -- ``SyntheticDecodeRunner`` tokens and logits
@@ -188,6 +190,27 @@ def _append_case(ikl):
                         layer=np.array(1), k_after=_np(cache.k), v_after=_np(cache.v))
 
 
+def _rotary_case(ikl):
+    hf = ikl["hf_benchmark"]
+    gen = torch.Generator().manual_seed(77)
+    out = {}
+    tokens, hq, hkv, dim = 37, 8, 2, 64
+    positions = torch.randint(0, 8192, (tokens,), generator=gen).double()
+    inv_freq = 1.0 / (500000.0 ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
+    angles = positions[:, None] * inv_freq[None, :]
+    emb = torch.cat((angles, angles), dim=-1)
+    for dtype in (torch.float16, torch.bfloat16):
+        kind = _KIND[dtype]
+        query = (torch.randn(tokens, hq, dim, generator=gen) * 3).to(dtype)
+        key = (torch.randn(tokens, hkv, dim, generator=gen) * 3).to(dtype)
+        cos, sin = emb.cos().to(dtype), emb.sin().to(dtype)
+        q_rot, k_rot = hf._apply_rotary(query, key, cos, sin)
+        for name, t in (("query", query), ("key", key), ("cos", cos), ("sin", sin),
+                        ("q_rot", q_rot), ("k_rot", k_rot)):
+            out[f"{kind}_{name}"] = _np(t)
+    np.savez_compressed(HERE / "rotary.npz", **out)
+
+
 def _runtime_traces(ikl):
     cache_mod = ikl["cache"]
     runtime_mod = ikl["runtime"]
@@ -276,12 +299,13 @@ def main() -> None:
     import importlib
 
     ikl = {m: importlib.import_module(f"inferkernellab.{m}")
-           for m in ("cache", "attention", "runtime", "scheduler", "decode")}
+           for m in ("cache", "attention", "runtime", "scheduler", "decode", "hf_benchmark")}
     torch.set_num_threads(4)
     _slot_cases(ikl)
     _decode_cases(ikl)
     _prefill_cases(ikl)
     _append_case(ikl)
+    _rotary_case(ikl)
     _runtime_traces(ikl)
     _synthetic_cases(ikl)
     print("golden fixtures written to", HERE)

@@ -67,6 +67,16 @@ def test_append_oracle_matches_reference():
     np.testing.assert_array_equal(v.view(np.uint16), d["v_after"].view(np.uint16))
 
 
+@pytest.mark.parametrize("kind", ["f16", "bf16"])
+def test_rotary_oracle_matches_reference_bit_exact(kind):
+    """The rounded-elementwise rotary restatement equals the reference's
+    ``_apply_rotary`` output bit for bit (hf_benchmark.py:69-85)."""
+    d = np.load(GOLDEN / "rotary.npz")
+    for src, want in (("query", "q_rot"), ("key", "k_rot")):
+        got = oracle.rotary_embed(d[f"{kind}_{src}"], d[f"{kind}_cos"], d[f"{kind}_sin"], kind)
+        np.testing.assert_array_equal(got.view(np.uint16), d[f"{kind}_{want}"].view(np.uint16))
+
+
 def test_bf16_round_trip_is_exact_and_rounds_to_nearest_even():
     bits = np.arange(0, 1 << 16, 7, dtype=np.uint16)
     f = oracle.bf16_bits_to_f32(bits)
