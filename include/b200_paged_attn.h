@@ -186,6 +186,29 @@ B200_API int b200_rope_append_kv(const b200_cache_desc* cache, const b200_rope_a
                                  const void* cos, const void* sin, const void* slots,
                                  void* query_out, uint32_t* error_word, void* stream);
 
+/* ------------------------------------------------- decoder-layer helpers
+ * Kernels for the Llama layer around the attention call (the reference's
+ * LlamaPagedDecodeRunner applies Transformers' LlamaRMSNorm and LlamaMLP
+ * modules there, reference hf_benchmark.py:408-511; these have no kernel
+ * counterpart in the reference).  dtype is B200_F16 or B200_BF16; strides are
+ * row strides in elements; 16-byte aligned rows with cols % 8 == 0 take the
+ * vectorised path.
+ *
+ * b200_add_rmsnorm: with x != NULL, residual_out = rnd(x + residual) (may alias
+ * residual); then out = rnd(weight * rnd(s * rsqrt(mean(s^2) + eps))) where s is
+ * the summed row (or residual itself when x == NULL) -- LlamaRMSNorm's
+ * roundings, one launch (one CTA per row).
+ * b200_silu_mul: gate_up rows hold [gate | up] (cols each);
+ * out = rnd(rnd(silu(gate)) * up) -- LlamaMLP's act_fn(gate) * up.
+ */
+B200_API int b200_add_rmsnorm(const void* x, const void* residual, const void* weight, void* out,
+                              void* residual_out, int64_t rows, int64_t cols, int64_t x_stride,
+                              int64_t residual_stride, int64_t out_stride,
+                              int64_t residual_out_stride, float eps, int32_t dtype, void* stream);
+
+B200_API int b200_silu_mul(const void* gate_up, void* out, int64_t rows, int64_t cols,
+                           int64_t in_stride, int64_t out_stride, int32_t dtype, void* stream);
+
 /* ----------------------------------------------------------------- prefill
  * Ragged causal prefill attention over the paged cache.  Sequence b owns the
  * query tokens of logical positions query_starts[b] .. context_lens[b]-1; a

@@ -20,6 +20,7 @@ build it with ``python -m inferkernellab_b200.build``.
 
 from .cache import BlockAllocator, CacheLayout, PagedKVCache
 from .ops import (
+    add_rmsnorm,
     append_kv,
     b200_available,
     build_slot_mapping,
@@ -28,6 +29,7 @@ from .ops import (
     paged_prefill_attention,
     paged_prefill_attention_varlen,
     rope_append_kv,
+    silu_mul,
 )
 from .runtime import InferenceRuntime, RuntimeStats
 from .scheduler import InferenceRequest, ScheduleBatch, TokenBudgetScheduler
@@ -51,6 +53,7 @@ __all__ = [
     "RuntimeStats",
     "ScheduleBatch",
     "TokenBudgetScheduler",
+    "add_rmsnorm",
     "append_kv",
     "append_kv_b200",
     "b200_available",
@@ -62,4 +65,5 @@ __all__ = [
     "paged_prefill_attention_b200",
     "paged_prefill_attention_varlen",
     "rope_append_kv",
+    "silu_mul",
 ]

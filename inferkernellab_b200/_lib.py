@@ -41,6 +41,8 @@ EXPORTED_SYMBOLS = (
     "b200_paged_decode_noalloc_scratch_bytes",
     "b200_append_kv",
     "b200_rope_append_kv",
+    "b200_add_rmsnorm",
+    "b200_silu_mul",
     "b200_paged_prefill",
     "b200_build_slot_mapping",
     "b200_validate_decode_metadata",
@@ -138,6 +140,9 @@ _PROTOTYPES = {
     "b200_rope_append_kv": (ctypes.c_int, [ctypes.POINTER(CacheDesc),
                                            ctypes.POINTER(RopeAppendArgs), _vp, _vp, _vp, _vp,
                                            _vp, _vp, _vp, _vp, _vp]),
+    "b200_add_rmsnorm": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                        _i64, ctypes.c_float, _i32, _vp]),
+    "b200_silu_mul": (ctypes.c_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
     "b200_paged_prefill": (ctypes.c_int, [ctypes.POINTER(CacheDesc), ctypes.POINTER(PrefillArgs),
                                           _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_build_slot_mapping": (ctypes.c_int, [_vp, _i32, _i64, _i32, _vp, _vp, _i32, _i32, _i32,

@@ -10,6 +10,7 @@
 #include "append.h"
 #include "decode.h"
 #include "host_common.h"
+#include "layer_ops.h"
 #include "metadata.h"
 #include "prefill.h"
 #include "rope_append.h"
@@ -85,6 +86,25 @@ int b200_rope_append_kv(const b200_cache_desc* cache, const b200_rope_append_arg
   return guarded([&] {
     return b200::launch_rope_append(cache, args, query, key, value, cos, sin, slots, query_out,
                                     error_word, as_stream(stream));
+  });
+}
+
+int b200_add_rmsnorm(const void* x, const void* residual, const void* weight, void* out,
+                     void* residual_out, int64_t rows, int64_t cols, int64_t x_stride,
+                     int64_t residual_stride, int64_t out_stride, int64_t residual_out_stride,
+                     float eps, int32_t dtype, void* stream) {
+  return guarded([&] {
+    return b200::launch_add_rmsnorm(x, residual, weight, out, residual_out, rows, cols, x_stride,
+                                    residual_stride, out_stride, residual_out_stride, eps, dtype,
+                                    as_stream(stream));
+  });
+}
+
+int b200_silu_mul(const void* gate_up, void* out, int64_t rows, int64_t cols, int64_t in_stride,
+                  int64_t out_stride, int32_t dtype, void* stream) {
+  return guarded([&] {
+    return b200::launch_silu_mul(gate_up, out, rows, cols, in_stride, out_stride, dtype,
+                                 as_stream(stream));
   });
 }
 

@@ -263,11 +263,13 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   __syncthreads();
 
   // Requests with no readable token: NaN, like 0/0 in the reference kernel.
+  // Each consumer thread of CTA 0 checks its share of the requests (this CTA
+  // must not spend a serial pass over the batch before it starts streaming).
   if (blockIdx.x == 0 && warp < kDecConsumerWarps) {
-    for (int r = 0; r < B; ++r) {
+    for (int r = tid; r < B; r += kConsumers) {
       if (len_s[r] != 0) continue;
       const int nh = HKV * G;
-      for (int i = tid; i < nh * D; i += kConsumers) {
+      for (int i = 0; i < nh * D; ++i) {
         const int hq = i / D, d = i - hq * D;
         reinterpret_cast<T*>(p.out)[r * p.out_stride_seq + hq * p.out_stride_head + d] =
             from_float<E>(__int_as_float(0x7fc00000));
@@ -526,13 +528,16 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
         }
       }
       if (!complete) {
-        __threadfence();
         named_bar_sync(1, kConsumers);
         const int p_first = seg_begin / per_cta;
         const int npieces = (seg_end_tile - 1) / per_cta - p_first + 1;
         if (tid == 0) {
           int last = 0;
-          if (!aborted) last = atomicAdd(&p.counters[seg], 1) == npieces - 1;
+          if (!aborted) {
+            __threadfence();  // release this CTA's piece (ordered after the barrier)
+            last = atomicAdd(&p.counters[seg], 1) == npieces - 1;
+            if (last) __threadfence();  // acquire the other pieces
+          }
           *merge_flag = last;
         }
         named_bar_sync(1, kConsumers);
@@ -540,26 +545,41 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
           // Last piece in: merge all pieces of the segment.  Piece i was written
           // by CTA q = p_first + i into slot 2q (segment began at or before q's
           // range) or 2q+1 (it began inside q's range).
-          __threadfence();
           auto piece_slot = [&](int i) {
             const int q = p_first + i;
             return seg_begin <= q * per_cta ? 2 * q : 2 * q + 1;
           };
+          // One pass over the pieces' lse: running max and rescaled sum per lane,
+          // then combined across the warp.  With few pieces the lse values stay
+          // in merge_w for the weights below (no second global read).
+          const bool lse_cached = npieces <= kMergeChunk;
           for (int row = warp; row < G; row += kDecConsumerWarps) {
-            float mmax = -INFINITY;
-            for (int i = lane; i < npieces; i += 32)
-              mmax = fmaxf(mmax, __ldcg(p.part_lse + piece_slot(i) * G + row));
-            mmax = warp_max(mmax);
-            const float base = mmax == -INFINITY ? 0.f : mmax;
-            float wsum = 0.f;
+            float m = -INFINITY, sum = 0.f;
             for (int i = lane; i < npieces; i += 32) {
               const float lse = __ldcg(p.part_lse + piece_slot(i) * G + row);
-              if (lse != -INFINITY) wsum += fast_exp2(lse - base);
+              if (lse_cached) merge_w[i * G + row] = lse;
+              if (lse == -INFINITY) continue;
+              if (lse > m) {
+                sum = (m == -INFINITY ? 0.f : sum * fast_exp2(m - lse)) + 1.f;
+                m = lse;
+              } else {
+                sum += fast_exp2(lse - m);
+              }
             }
-            wsum = warp_sum(wsum);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+              const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+              const float s2 = __shfl_xor_sync(0xffffffffu, sum, o);
+              const float mm = fmaxf(m, m2);
+              if (mm != -INFINITY) {
+                sum = (m == -INFINITY ? 0.f : sum * fast_exp2(m - mm)) +
+                      (m2 == -INFINITY ? 0.f : s2 * fast_exp2(m2 - mm));
+                m = mm;
+              }
+            }
             if (lane == 0) {
-              row_base[row] = base;
-              row_l[row] = 1.f / wsum;
+              row_base[row] = m == -INFINITY ? 0.f : m;
+              row_l[row] = 1.f / sum;
             }
           }
           named_bar_sync(1, kConsumers);
@@ -573,7 +593,8 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
               const int row = i - q * G;
               float w = 0.f;
               if (q < nq) {
-                const float lse = __ldcg(p.part_lse + piece_slot(c0 + q) * G + row);
+                const float lse =
+                    lse_cached ? merge_w[i] : __ldcg(p.part_lse + piece_slot(c0 + q) * G + row);
                 if (lse != -INFINITY) w = fast_exp2(lse - row_base[row]) * row_l[row];
               }
               merge_w[i] = w;

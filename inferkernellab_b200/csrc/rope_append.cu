@@ -55,21 +55,41 @@ __device__ __forceinline__ float rnd(float x) {
   return to_f<E>(from_float<E>(x));
 }
 
+// 8 x 16-bit elements = one 16-byte access.
+struct alignas(16) Vec8 {
+  uint16_t h[8];
+};
+
 template <typename E>
+__device__ __forceinline__ float lane_f(const Vec8& v, int i) {
+  typename E::T t;
+  memcpy(&t, &v.h[i], 2);
+  return to_f<E>(t);
+}
+
+template <typename E>
+__device__ __forceinline__ void lane_set(Vec8& v, int i, float x) {
+  typename E::T t = from_float<E>(x);
+  memcpy(&v.h[i], &t, 2);
+}
+
+// One work item = W consecutive pair indices i..i+W-1 of one row (W = 8 with
+// 16-byte vectors, else 1).  Rows per token: q heads, then k heads (rotated),
+// then v heads (copied).
+template <typename E, int W>
 __global__ void __launch_bounds__(256) rope_append_kernel(const RopeParams p) {
   using T = typename E::T;
   const int half = p.head_dim / 2;
-  // Work items per token: rotated rows (q heads, then k heads) x half-pairs,
-  // then V rows x half-pairs (two elements copied per item).
+  const int items_per_row = half / W;
   const int rot_rows = p.num_q_heads + p.num_kv_heads;
-  const long long per_token = static_cast<long long>(rot_rows + p.num_kv_heads) * half;
+  const long long per_token = static_cast<long long>(rot_rows + p.num_kv_heads) * items_per_row;
   const long long total = p.num_tokens * per_token;
   for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long t = idx / per_token;
     const int rem = static_cast<int>(idx - t * per_token);
-    const int row = rem / half;
-    const int i = rem - row * half;
+    const int row = rem / items_per_row;
+    const int i = (rem - row * items_per_row) * W;
     const bool is_q = row < p.num_q_heads;
     const bool is_k = !is_q && row < rot_rows;
     long long slot = 0;
@@ -81,40 +101,64 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeParams p) {
         continue;
       }
     }
-    if (is_q || is_k) {
-      const T* src;
-      if (is_q)
-        src = reinterpret_cast<const T*>(p.q) + t * p.q_st + row * p.q_sh;
-      else
-        src = reinterpret_cast<const T*>(p.k) + t * p.k_st + (row - p.num_q_heads) * p.k_sh;
-      const T* c = reinterpret_cast<const T*>(p.cos) + t * p.cos_st;
-      const T* s = reinterpret_cast<const T*>(p.sin) + t * p.sin_st;
-      const float x1 = to_f<E>(src[i]);
-      const float x2 = to_f<E>(src[i + half]);
-      // first half: x1*cos - x2*sin ; second half: x2*cos + x1*sin (rounded like torch)
-      const float lo = rnd<E>(rnd<E>(x1 * to_f<E>(c[i])) + rnd<E>(-x2 * to_f<E>(s[i])));
-      const float hi =
-          rnd<E>(rnd<E>(x2 * to_f<E>(c[i + half])) + rnd<E>(x1 * to_f<E>(s[i + half])));
-      T* dst;
-      if (is_q) {
-        dst = reinterpret_cast<T*>(p.q_out) + t * p.qo_st + row * p.qo_sh;
-      } else {
-        const int h = row - p.num_q_heads;
-        dst = reinterpret_cast<T*>(p.k_cache) +
-              ((p.layer_slot_base + slot) * p.num_kv_heads + h) * p.head_dim;
-      }
-      dst[i] = from_float<E>(lo);
-      dst[i + half] = from_float<E>(hi);
+    const T* src;
+    T* dst;
+    if (is_q) {
+      src = reinterpret_cast<const T*>(p.q) + t * p.q_st + row * p.q_sh;
+      dst = reinterpret_cast<T*>(p.q_out) + t * p.qo_st + row * p.qo_sh;
+    } else if (is_k) {
+      const int h = row - p.num_q_heads;
+      src = reinterpret_cast<const T*>(p.k) + t * p.k_st + h * p.k_sh;
+      dst = reinterpret_cast<T*>(p.k_cache) +
+            ((p.layer_slot_base + slot) * p.num_kv_heads + h) * p.head_dim;
     } else {
       const int h = row - rot_rows;
-      const T* src = reinterpret_cast<const T*>(p.v) + t * p.v_st + h * p.v_sh;
-      T* dst = reinterpret_cast<T*>(p.v_cache) +
-               ((p.layer_slot_base + slot) * p.num_kv_heads + h) * p.head_dim;
-      dst[i] = src[i];
-      dst[i + half] = src[i + half];
+      src = reinterpret_cast<const T*>(p.v) + t * p.v_st + h * p.v_sh;
+      dst = reinterpret_cast<T*>(p.v_cache) +
+            ((p.layer_slot_base + slot) * p.num_kv_heads + h) * p.head_dim;
+    }
+    if (W == 8) {
+      const Vec8 x1 = *reinterpret_cast<const Vec8*>(src + i);
+      const Vec8 x2 = *reinterpret_cast<const Vec8*>(src + i + half);
+      if (!(is_q || is_k)) {
+        *reinterpret_cast<Vec8*>(dst + i) = x1;
+        *reinterpret_cast<Vec8*>(dst + i + half) = x2;
+        continue;
+      }
+      const T* c = reinterpret_cast<const T*>(p.cos) + t * p.cos_st;
+      const T* s = reinterpret_cast<const T*>(p.sin) + t * p.sin_st;
+      const Vec8 c1 = *reinterpret_cast<const Vec8*>(c + i);
+      const Vec8 c2 = *reinterpret_cast<const Vec8*>(c + i + half);
+      const Vec8 s1 = *reinterpret_cast<const Vec8*>(s + i);
+      const Vec8 s2 = *reinterpret_cast<const Vec8*>(s + i + half);
+      Vec8 lo, hi;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float a = lane_f<E>(x1, j), b = lane_f<E>(x2, j);
+        // first half: a*cos - b*sin ; second half: b*cos + a*sin (rounded like torch)
+        lane_set<E>(lo, j, rnd<E>(a * lane_f<E>(c1, j)) + rnd<E>(-b * lane_f<E>(s1, j)));
+        lane_set<E>(hi, j, rnd<E>(b * lane_f<E>(c2, j)) + rnd<E>(a * lane_f<E>(s2, j)));
+      }
+      *reinterpret_cast<Vec8*>(dst + i) = lo;
+      *reinterpret_cast<Vec8*>(dst + i + half) = hi;
+    } else {
+      if (!(is_q || is_k)) {
+        dst[i] = src[i];
+        dst[i + half] = src[i + half];
+        continue;
+      }
+      const T* c = reinterpret_cast<const T*>(p.cos) + t * p.cos_st;
+      const T* s = reinterpret_cast<const T*>(p.sin) + t * p.sin_st;
+      const float a = to_f<E>(src[i]);
+      const float b = to_f<E>(src[i + half]);
+      dst[i] = from_float<E>(rnd<E>(a * to_f<E>(c[i])) + rnd<E>(-b * to_f<E>(s[i])));
+      dst[i + half] =
+          from_float<E>(rnd<E>(b * to_f<E>(c[i + half])) + rnd<E>(a * to_f<E>(s[i + half])));
     }
   }
 }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int launch_rope_append(const b200_cache_desc* c, const b200_rope_append_args* a, const void* query,
                        const void* key, const void* value, const void* cos, const void* sin,
@@ -164,14 +208,30 @@ int launch_rope_append(const b200_cache_desc* c, const b200_rope_append_args* a,
   p.num_kv_heads = c->num_kv_heads;
   p.head_dim = c->head_dim;
   p.slots64 = a->slots_dtype == B200_I64;
+  // 16-byte vectors need every row start and both halves 16-byte aligned.
+  const bool vec = c->head_dim % 16 == 0 && p.q_st % 8 == 0 && p.q_sh % 8 == 0 &&
+                   p.k_st % 8 == 0 && p.k_sh % 8 == 0 && p.v_st % 8 == 0 && p.v_sh % 8 == 0 &&
+                   p.qo_st % 8 == 0 && p.qo_sh % 8 == 0 && p.cos_st % 8 == 0 &&
+                   p.sin_st % 8 == 0 && aligned16(query) && aligned16(key) && aligned16(value) &&
+                   aligned16(cos) && aligned16(sin) && aligned16(query_out) &&
+                   aligned16(c->k_cache) && aligned16(c->v_cache);
+  const int width = vec ? 8 : 1;
   const long long work =
-      a->num_tokens * (a->num_q_heads + 2LL * c->num_kv_heads) * (c->head_dim / 2);
+      a->num_tokens * (a->num_q_heads + 2LL * c->num_kv_heads) * (c->head_dim / 2 / width);
   long long blocks = (work + 255) / 256;
   if (blocks > 148LL * 32) blocks = 148LL * 32;
-  if (c->dtype == B200_BF16)
-    rope_append_kernel<BF16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
-  else
-    rope_append_kernel<Half><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
+  const unsigned b = static_cast<unsigned>(blocks);
+  if (c->dtype == B200_BF16) {
+    if (vec)
+      rope_append_kernel<BF16, 8><<<b, 256, 0, stream>>>(p);
+    else
+      rope_append_kernel<BF16, 1><<<b, 256, 0, stream>>>(p);
+  } else {
+    if (vec)
+      rope_append_kernel<Half, 8><<<b, 256, 0, stream>>>(p);
+    else
+      rope_append_kernel<Half, 1><<<b, 256, 0, stream>>>(p);
+  }
   return cuda_status(cudaGetLastError(), "rope_append_kernel launch");
 }
 

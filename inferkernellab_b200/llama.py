@@ -2,11 +2,21 @@
 
 Mirror of the reference's ``LlamaPagedDecodeRunner`` / ``LlamaPagedRunResult``
 (reference ``src/inferkernellab/hf_benchmark.py:88-695``) for backend
-``"b200_paged"`` / append ``"b200"``.  Every non-attention op is the model's own
-Transformers module (RMSNorm, q/k/v/o projections, rotary embedding, SiLU MLP,
-final norm, lm_head), applied exactly as the reference does, so logits differ
-from the eager model only through attention arithmetic.  Attention-side work is
-on the sm_100a kernels:
+``"b200_paged"`` / append ``"b200"``.  The layer computes what the reference's
+Transformers modules compute, with the launches cut down:
+
+* the q/k/v projections run as one GEMM over a packed ``[q | k | v]`` weight
+  and gate/up as one GEMM over ``[gate | up]``; the model's own ``Linear``
+  weights are re-pointed at views of the packed tensors, so the model keeps
+  working unchanged and no weight memory is duplicated;
+* every ``LlamaRMSNorm`` (with the residual add in front of it) is one
+  ``add_rmsnorm`` launch and ``act_fn(gate) * up`` one ``silu_mul`` launch,
+  both rounding like the torch ops they replace;
+* o_proj, down_proj, the embedding, the rotary table and lm_head are the
+  model's own modules.
+
+Logits therefore differ from the eager model only through attention and GEMM
+summation order.  Attention-side work is on the sm_100a kernels:
 
 * batched prefill is *packed*: the scheduled ranges of a budget batch are
   concatenated (no padding rows, unlike the reference's ``_prefill_batch``
@@ -43,10 +53,12 @@ import torch
 from .cache import PagedKVCache
 from .decode import DeviceBlockTables, _percentile
 from .ops import (
+    add_rmsnorm,
     build_slot_mapping,
     paged_decode_attention,
     paged_prefill_attention_varlen,
     rope_append_kv,
+    silu_mul,
 )
 from .runtime import InferenceRuntime
 from .scheduler import InferenceRequest, TokenBudgetScheduler
@@ -168,6 +180,7 @@ class LlamaPagedDecodeRunner:
         self.meta = DeviceBlockTables(len(self.requests), width, self.device)
         self._prompt_logits: dict[int, torch.Tensor] = {}
         self._next_logits: dict[int, torch.Tensor] = {}
+        self._batch_logits: tuple[tuple[int, ...], torch.Tensor] | None = None
         self._decode_logits: list[torch.Tensor] = []
         self._generated: dict[int, list[int]] = {r.request_id: [] for r in self.requests}
         self._token_logprobs: dict[int, list[float]] = {r.request_id: [] for r in self.requests}
@@ -179,41 +192,59 @@ class LlamaPagedDecodeRunner:
             gen.manual_seed(seed + r.request_id)
             self._generators[r.request_id] = gen
         self._has_run = False
+        self._pack_weights()
 
     # ------------------------------------------------------------------ layers
-    def _layer_qkv(self, layer, hidden, tokens: int):
-        attn = layer.self_attn
-        q = attn.q_proj(hidden).view(tokens, self.num_heads, self.head_dim)
-        k = attn.k_proj(hidden).view(tokens, self.num_kv_heads, self.head_dim)
-        v = attn.v_proj(hidden).view(tokens, self.num_kv_heads, self.head_dim)
-        return q, k, v
+    def _pack_weights(self) -> None:
+        """Pack each layer's q/k/v and gate/up weights into one tensor each.
 
-    def _layer_tail(self, layer, residual, attended, tokens: int):
-        hidden = residual + layer.self_attn.o_proj(attended.reshape(tokens, -1))
-        residual = hidden
-        hidden = layer.post_attention_layernorm(hidden)
-        hidden = layer.mlp.down_proj(layer.mlp.act_fn(layer.mlp.gate_proj(hidden))
-                                     * layer.mlp.up_proj(hidden))
-        return residual + hidden
+        The model's ``Linear`` modules are re-pointed at views of the packed
+        tensors (same values), so the eager model still works and the weights
+        are not held twice."""
+        act = getattr(self.model.config, "hidden_act", "silu")
+        if act != "silu":
+            raise ValueError(f"the b200 runner supports SiLU-gated MLPs, not {act!r}")
+        self._qkv, self._gate_up = [], []
+        for layer in self.model.model.layers:
+            attn, mlp = layer.self_attn, layer.mlp
+            self._qkv.append(_pack_linears((attn.q_proj, attn.k_proj, attn.v_proj)))
+            self._gate_up.append(_pack_linears((mlp.gate_proj, mlp.up_proj)))
 
     def _forward(self, token_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
                  attend) -> torch.Tensor:
-        """Shared layer loop on a flat token batch ``[N]``; returns hidden ``[N, H]``.
+        """Shared layer loop on a flat token batch ``[N]``; returns the final-norm
+        hidden ``[N, H]``.
 
-        Per layer: projections, then one ``rope_append_kv`` (rotary on q/k and
-        K/V into ``slots``), then ``attend(layer, rotated_q)``."""
+        Per layer: one q|k|v GEMM, one ``rope_append_kv`` (rotary on q/k, K/V
+        into ``slots``), ``attend(layer, rotated_q)``, o_proj, ``add_rmsnorm``
+        (residual add + post-attention norm), one gate|up GEMM, ``silu_mul``,
+        down_proj and ``add_rmsnorm`` into the next layer's input norm."""
         n = token_ids.shape[0]
-        hidden = self.model.model.embed_tokens(token_ids.to(torch.long))
-        cos, sin = self.model.model.rotary_emb(hidden.unsqueeze(0), positions.view(1, -1))
+        inner = self.model.model
+        hidden = inner.embed_tokens(token_ids.to(torch.long))
+        cos, sin = inner.rotary_emb(hidden.unsqueeze(0), positions.view(1, -1))
         cos, sin = cos[0], sin[0]
-        for index, layer in enumerate(self.model.model.layers):
-            residual = hidden
-            hidden = layer.input_layernorm(hidden)
-            q, k, v = self._layer_qkv(layer, hidden, n)
+        layers = inner.layers
+        qd = self.num_heads * self.head_dim
+        kvd = self.num_kv_heads * self.head_dim
+        normed, residual = add_rmsnorm(None, hidden, *_norm_args(layers[0].input_layernorm))
+        for index, layer in enumerate(layers):
+            weight, bias = self._qkv[index]
+            qkv = torch.nn.functional.linear(normed, weight, bias)
+            q = qkv[:, :qd].view(n, self.num_heads, self.head_dim)
+            k = qkv[:, qd:qd + kvd].view(n, self.num_kv_heads, self.head_dim)
+            v = qkv[:, qd + kvd:].view(n, self.num_kv_heads, self.head_dim)
             q = rope_append_kv(q, k, v, cos, sin, self.cache, slots, layer=index)
             attended = attend(index, q)
-            hidden = self._layer_tail(layer, residual, attended, n)
-        return self.model.model.norm(hidden)
+            out = layer.self_attn.o_proj(attended.reshape(n, qd))
+            normed, residual = add_rmsnorm(out, residual,
+                                           *_norm_args(layer.post_attention_layernorm))
+            weight, bias = self._gate_up[index]
+            act = silu_mul(torch.nn.functional.linear(normed, weight, bias))
+            out = layer.mlp.down_proj(act)
+            following = layers[index + 1].input_layernorm if index + 1 < len(layers) else inner.norm
+            normed, residual = add_rmsnorm(out, residual, *_norm_args(following))
+        return normed
 
     def _decode_body(self, token_ids: torch.Tensor, positions: torch.Tensor,
                      tables: torch.Tensor) -> torch.Tensor:
@@ -307,8 +338,23 @@ class LlamaPagedDecodeRunner:
         return (token, policy_logprobs.gather(-1, token.view(1)).squeeze(0),
                 log_probs.gather(-1, token.view(1)).squeeze(0))
 
+    def _logits_for(self, requests) -> torch.Tensor:
+        """``[B, V]`` next-token logits of ``requests``: the previous decode step's
+        batch tensor as is when the batch is unchanged, else gathered per request."""
+        ids = tuple(r.request_id for r in requests)
+        if self._batch_logits is not None:
+            batch_ids, logits = self._batch_logits
+            if batch_ids == ids:
+                return logits
+            for row, rid in enumerate(batch_ids):
+                self._next_logits[rid] = logits[row].clone()
+            self._batch_logits = None
+        return torch.stack([self._next_logits[rid] for rid in ids], dim=0)
+
     def _decode(self, requests: tuple[InferenceRequest, ...]) -> None:
-        used = torch.stack([self._next_logits[r.request_id] for r in requests], dim=0)
+        used = self._logits_for(requests)
+        if self.collect_logits:
+            self._decode_logits.append(used.detach().float().cpu())
         sampled = None
         if self.temperature == 0 and not self.eos_token_ids:
             next_tokens = used.argmax(dim=-1).to(torch.long)
@@ -327,8 +373,6 @@ class LlamaPagedDecodeRunner:
             next_logits = self._graph.replay(next_tokens, positions)
         else:
             next_logits = self._forward_decode(next_tokens, requests, positions)
-        if self.collect_logits:
-            self._decode_logits.append(used.detach().float().cpu())
         tokens = next_tokens.tolist()
         for row, request in enumerate(requests):
             token = int(tokens[row])
@@ -339,7 +383,7 @@ class LlamaPagedDecodeRunner:
             if token in self.eos_token_ids:
                 self._finish_reasons[request.request_id] = "eos"
                 request.max_new_tokens = request.generated_tokens + 1
-            self._next_logits[request.request_id] = next_logits[row].detach()
+        self._batch_logits = (tuple(ids), next_logits.detach())
 
     # --------------------------------------------------------------------- run
     def _timed_step(self):
@@ -438,6 +482,33 @@ class _DecodeGraph:
 
 
 # ------------------------------------------------------------------ helpers
+
+def _pack_linears(modules) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Concatenate ``Linear`` weights (and biases) along the output dimension and
+    re-point each module's parameters at its slice of the packed tensors."""
+    biases = [m.bias for m in modules]
+    if any(b is None for b in biases) and not all(b is None for b in biases):
+        raise ValueError("cannot pack projections where only some have a bias")
+    with torch.no_grad():
+        weight = torch.cat([m.weight.detach() for m in modules], dim=0).contiguous()
+        bias = None if biases[0] is None else torch.cat([b.detach() for b in biases]).contiguous()
+        offset = 0
+        for m in modules:
+            rows = m.weight.shape[0]
+            m.weight = torch.nn.Parameter(weight[offset:offset + rows], requires_grad=False)
+            if bias is not None:
+                m.bias = torch.nn.Parameter(bias[offset:offset + rows], requires_grad=False)
+            offset += rows
+    return weight, bias
+
+
+def _norm_args(norm) -> tuple[torch.Tensor, float]:
+    """(weight, eps) of a ``LlamaRMSNorm``."""
+    eps = getattr(norm, "variance_epsilon", None)
+    if eps is None:
+        eps = getattr(norm, "eps")
+    return norm.weight, float(eps)
+
 
 def load_random_llama(*, vocab_size: int, hidden_size: int, intermediate_size: int,
                       num_layers: int, num_attention_heads: int, num_kv_heads: int,

@@ -13,6 +13,9 @@ this module                            reference (``src/inferkernellab/``)
 ``paged_prefill_attention``            ``attention.paged_prefill_attention_sdpa`` (:230-321)
 ``paged_prefill_attention_varlen``     (new) packed ``[sum T, Hq, D]`` form over ``cu_seqlens``
 ``build_slot_mapping``                 (new) device form of ``PagedKVCache.slot_mapping`` for a batch
+``rope_append_kv``                     ``hf_benchmark._apply_rotary`` (:69-85) + ``append_kv_triton``
+``add_rmsnorm`` / ``silu_mul``         (new) Transformers ``LlamaRMSNorm`` (+ residual add) and the
+                                       ``act_fn(gate) * up`` of ``LlamaMLP``, one launch each
 =====================================  ==========================================================
 
 All launches go on torch's current CUDA stream through the C ABI in
@@ -354,6 +357,73 @@ def rope_append_kv(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
         ctypes.byref(desc), ctypes.byref(args), query.data_ptr(), key.data_ptr(),
         value.data_ptr(), cos.data_ptr(), sin.data_ptr(), slots.data_ptr(), out.data_ptr(),
         _ERROR_WORDS.get(device).data_ptr(), _stream_ptr(device)))
+    return out
+
+
+# ------------------------------------------------------------- layer helpers
+
+def _rows2d(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.ndim != 2:
+        raise ValueError(f"{name} must be a 2-D [rows, cols] tensor")
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def add_rmsnorm(x: torch.Tensor | None, residual: torch.Tensor, weight: torch.Tensor,
+                eps: float, *, out: torch.Tensor | None = None,
+                residual_out: torch.Tensor | None = None):
+    """``LlamaRMSNorm(residual + x)`` in one launch; returns ``(normed, summed)``.
+
+    With ``x`` given, the rounded sum ``residual + x`` is written to
+    ``residual_out`` (default: in place into ``residual``) and normalised;
+    with ``x=None`` ``residual`` itself is normalised and returned as
+    ``summed``.  ``[rows, cols]`` tensors in the weight's 16-bit dtype.
+    """
+    residual = _rows2d(residual, "residual")
+    rows, cols = residual.shape
+    device, dtype = residual.device, residual.dtype
+    if device.type != "cuda" or dtype not in _DTYPE_CODE:
+        raise ValueError("add_rmsnorm needs float16/bfloat16 CUDA tensors")
+    if weight.shape != (cols,) or weight.dtype != dtype or weight.device != device:
+        raise ValueError("weight must be [cols] with the residual's dtype and device")
+    weight = weight.contiguous()
+    if x is not None:
+        x = _rows2d(x, "x")
+        if x.shape != residual.shape or x.dtype != dtype or x.device != device:
+            raise ValueError("x must match residual's shape, dtype and device")
+        if residual_out is None:
+            residual_out = residual
+        elif (residual_out.shape != residual.shape or residual_out.dtype != dtype
+              or residual_out.stride(-1) != 1):
+            raise ValueError("residual_out must match residual")
+    if out is None:
+        out = torch.empty((rows, cols), dtype=dtype, device=device)
+    elif out.shape != (rows, cols) or out.dtype != dtype or out.stride(-1) != 1:
+        raise ValueError("out must be a [rows, cols] tensor of the residual's dtype")
+    _lib.check(_lib.load().b200_add_rmsnorm(
+        x.data_ptr() if x is not None else None, residual.data_ptr(), weight.data_ptr(),
+        out.data_ptr(), residual_out.data_ptr() if x is not None else None, rows, cols,
+        x.stride(0) if x is not None else 0, residual.stride(0), out.stride(0),
+        residual_out.stride(0) if x is not None else 0, float(eps), _DTYPE_CODE[dtype],
+        _stream_ptr(device)))
+    return out, (residual_out if x is not None else residual)
+
+
+def silu_mul(gate_up: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``silu(gate) * up`` for ``gate_up = [gate | up]`` rows ``[rows, 2 * I]``, one launch."""
+    gate_up = _rows2d(gate_up, "gate_up")
+    rows, width = gate_up.shape
+    if width % 2:
+        raise ValueError("gate_up must hold [gate | up] halves of equal width")
+    if gate_up.device.type != "cuda" or gate_up.dtype not in _DTYPE_CODE:
+        raise ValueError("silu_mul needs a float16/bfloat16 CUDA tensor")
+    cols = width // 2
+    if out is None:
+        out = torch.empty((rows, cols), dtype=gate_up.dtype, device=gate_up.device)
+    elif out.shape != (rows, cols) or out.dtype != gate_up.dtype or out.stride(-1) != 1:
+        raise ValueError("out must be [rows, I] in gate_up's dtype")
+    _lib.check(_lib.load().b200_silu_mul(
+        gate_up.data_ptr(), out.data_ptr(), rows, cols, gate_up.stride(0), out.stride(0),
+        _DTYPE_CODE[gate_up.dtype], _stream_ptr(gate_up.device)))
     return out
 
 

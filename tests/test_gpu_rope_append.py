@@ -154,3 +154,29 @@ def test_rope_append_flags_out_of_pool_slots_and_validates():
     empty = rope_append_kv(query[:0], key[:0], key[:0], cos[:0], sin[:0], cache,
                            torch.zeros(0, dtype=torch.int64, device="cuda"))
     assert empty.shape == (0, 4, 16)
+
+
+def test_rope_append_unaligned_views_take_the_scalar_path():
+    """Inputs that are not 16-byte aligned give the same bits as aligned ones."""
+    gen = torch.Generator().manual_seed(23)
+    dtype, tokens, hq, hkv, dim = torch.float16, 31, 8, 2, 64
+    a = PagedKVCache(8, 16, hkv, dim, dtype=dtype, device="cuda")
+    b = PagedKVCache(8, 16, hkv, dim, dtype=dtype, device="cuda")
+    for c in (a, b):
+        c.k.zero_()
+        c.v.zero_()
+    width = (hq + 2 * hkv) * dim
+    flat = torch.randn(tokens, width + 1, generator=gen).to(dtype).cuda()
+    qkv = flat[:, 1:]  # one-element offset: every row start is misaligned
+    query = qkv[:, : hq * dim].view(tokens, hq, dim)
+    key = qkv[:, hq * dim:(hq + hkv) * dim].view(tokens, hkv, dim)
+    value = qkv[:, (hq + hkv) * dim:].view(tokens, hkv, dim)
+    cos, sin = _rotary_table(torch.arange(tokens) * 37, dim, dtype)
+    cos, sin = cos.cuda(), sin.cuda()
+    slots = torch.randperm(128, generator=gen)[:tokens].cuda()
+    got = rope_append_kv(query, key, value, cos, sin, a, slots)
+    want = rope_append_kv(query.contiguous(), key.contiguous(), value.contiguous(), cos, sin, b,
+                          slots)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want) and torch.equal(got, _torch_rotary(query, cos, sin))
+    assert torch.equal(a.k, b.k) and torch.equal(a.v, b.v)
