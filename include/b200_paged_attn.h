@@ -186,6 +186,16 @@ B200_API int b200_rope_append_kv(const b200_cache_desc* cache, const b200_rope_a
                                  const void* cos, const void* sin, const void* slots,
                                  void* query_out, uint32_t* error_word, void* stream);
 
+/* ------------------------------------------------------- diagnostics
+ * b200_tc_selftest: one CTA checks the tcgen05 building blocks of the prefill
+ * kernel (128-byte swizzled K-major / MN-major shared-memory descriptors,
+ * kind::f16 MMAs into tensor memory, tcgen05.ld readback):
+ *   c1[128, 64]  = a[128, 64] . b[64, 64]^T,   c2[128, 128] = a[128, 64] . v[64, 128]
+ * a, b, v row-major 16-bit (dtype), 16-byte aligned; c1, c2 row-major float32.
+ * No counterpart in the reference. */
+B200_API int b200_tc_selftest(const void* a, const void* b, const void* v, float* c1, float* c2,
+                              int32_t dtype, uint32_t* error_word, void* stream);
+
 /* ------------------------------------------------- decoder-layer helpers
  * Kernels for the Llama layer around the attention call (the reference's
  * LlamaPagedDecodeRunner applies Transformers' LlamaRMSNorm and LlamaMLP
@@ -237,7 +247,14 @@ typedef struct {
   int32_t table_dtype; /* B200_I32 / B200_I64 */
   int32_t index_dtype; /* dtype of query_starts / context_lens */
   float scale;
+  int32_t kernel; /* B200_PREFILL_AUTO / _TCGEN05 / _MMA_SYNC */
 } b200_prefill_args;
+
+/* Prefill kernel choice.  AUTO takes the tcgen05 (TMEM) kernel for head_dim
+ * 64 / 128 on 128-byte swizzled cache tiles (block_size >= 8) and the
+ * mma.sync kernel otherwise; TCGEN05 fails with B200_ERR_UNSUPPORTED where it
+ * cannot run. */
+enum { B200_PREFILL_AUTO = 0, B200_PREFILL_TCGEN05 = 1, B200_PREFILL_MMA_SYNC = 2 };
 
 B200_API int b200_paged_prefill(const b200_cache_desc* cache, const b200_prefill_args* args,
                        const void* query, const void* block_tables, const void* query_starts,

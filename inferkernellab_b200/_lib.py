@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "b200_rope_append_kv",
     "b200_add_rmsnorm",
     "b200_silu_mul",
+    "b200_tc_selftest",
     "b200_paged_prefill",
     "b200_build_slot_mapping",
     "b200_validate_decode_metadata",
@@ -101,6 +102,7 @@ class PrefillArgs(ctypes.Structure):
         ("table_dtype", ctypes.c_int32),
         ("index_dtype", ctypes.c_int32),
         ("scale", ctypes.c_float),
+        ("kernel", ctypes.c_int32),
     ]
 
 
@@ -143,6 +145,7 @@ _PROTOTYPES = {
     "b200_add_rmsnorm": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                         _i64, ctypes.c_float, _i32, _vp]),
     "b200_silu_mul": (ctypes.c_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
+    "b200_tc_selftest": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp]),
     "b200_paged_prefill": (ctypes.c_int, [ctypes.POINTER(CacheDesc), ctypes.POINTER(PrefillArgs),
                                           _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_build_slot_mapping": (ctypes.c_int, [_vp, _i32, _i64, _i32, _vp, _vp, _i32, _i32, _i32,

@@ -224,8 +224,10 @@ def run_prefill(args) -> dict:
     dtype = torch.bfloat16
     hq, hkv, dim, bs = 32, 8, 128, 16
     gen = torch.Generator().manual_seed(args.seed)
-    lens = torch.randint(17, 513, (24,), generator=gen).tolist()
-    sched = TokenBudgetScheduler(max_num_seqs=32, max_num_batched_tokens=2048)
+    lens = torch.randint(args.prefill_min_len, args.prefill_max_len + 1, (args.prefill_prompts,),
+                         generator=gen).tolist()
+    sched = TokenBudgetScheduler(max_num_seqs=max(32, args.prefill_prompts),
+                                 max_num_batched_tokens=2048)
     reqs = [InferenceRequest(i, n, 1) for i, n in enumerate(lens)]
     for r in reqs:
         sched.add(r)
@@ -268,25 +270,44 @@ def run_prefill(args) -> dict:
             slots, cu = build_slot_mapping(btab, starts, ends, block_size=bs,
                                            num_blocks=num_blocks, total_tokens=total)
             append_kv(k, v, cache, slots)
-            paged_prefill_attention_varlen(q, cache, btab, cu, starts, ends)
+            paged_prefill_attention_varlen(q, cache, btab, cu, starts, ends,
+                                           kernel=args.prefill_kernel)
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.iterations):
-        step()
-    e1.record()
-    e1.synchronize()
-    ms = e0.elapsed_time(e1) / args.iterations
+    metas = []
+    for btab, starts, ends, total, q, k, v in work:
+        slots, cu = build_slot_mapping(btab, starts, ends, block_size=bs,
+                                       num_blocks=num_blocks, total_tokens=total)
+        metas.append(cu)
+
+    def attention_only():
+        for (btab, starts, ends, total, q, k, v), cu in zip(work, metas):
+            paged_prefill_attention_varlen(q, cache, btab, cu, starts, ends,
+                                           kernel=args.prefill_kernel)
+
+    def timed(fn) -> float:
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.iterations):
+            fn()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / args.iterations
+
+    ms = timed(step)
+    attn_ms = timed(attention_only)
     return {
         "schema_version": 2, "benchmark": "config4_prefill",
         "environment": _environment(device),
         "config": {"prompts": lens, "budget": 2048, "batches": len(batches), "num_heads": hq,
-                   "num_kv_heads": hkv, "head_dim": dim, "block_size": bs, "dtype": "bfloat16"},
+                   "num_kv_heads": hkv, "head_dim": dim, "block_size": bs, "dtype": "bfloat16",
+                   "kernel": args.prefill_kernel},
         "prefill_ms": ms, "causal_attention_flops": flops,
         "achieved_tflops": flops / (ms * 1e-3) / 1e12,
+        "attention_only_ms": attn_ms,
+        "attention_only_tflops": flops / (attn_ms * 1e-3) / 1e12,
         "tokens_per_s": sum(lens) / (ms * 1e-3),
     }
 
@@ -312,6 +333,10 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--sweep", choices=("config2",), default=None)
     p.add_argument("--prefill", action="store_true", help="config-4 ragged prefill benchmark")
+    p.add_argument("--prefill-kernel", choices=("auto", "tcgen05", "mma_sync"), default="auto")
+    p.add_argument("--prefill-prompts", type=int, default=24)
+    p.add_argument("--prefill-min-len", type=int, default=17)
+    p.add_argument("--prefill-max-len", type=int, default=512)
     p.add_argument("--profile-kernel", action="store_true",
                    help="one decode launch between cudaProfilerStart/Stop (ncu --profile-from-start off)")
     p.add_argument("--output", type=Path)

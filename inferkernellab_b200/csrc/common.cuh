@@ -147,9 +147,11 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
 // Element-type traits: 16-bit storage type and its mma.sync spelling.
 struct Half {
   using T = __half;
+  static constexpr bool kIsBf16 = false;
 };
 struct BF16 {
   using T = __nv_bfloat16;
+  static constexpr bool kIsBf16 = true;
 };
 
 template <typename E>

@@ -21,29 +21,13 @@
 #include "common.cuh"
 #include "host_common.h"
 #include "prefill.h"
+#include "prefill_params.h"
 
 namespace b200 {
 
 constexpr int kPreConsumerWarps = 4;
 constexpr int kPreThreads = (kPreConsumerWarps + 1) * 32;
 constexpr int kPreRows = kPreConsumerWarps * 16;  // query tokens per CTA
-constexpr int kPreMaxSeqs = 8192;
-
-struct PrefillParams {
-  const void* q;
-  void* out;
-  const void* starts;
-  const void* ends;
-  const int* cu_seqlens;
-  uint32_t* err;
-  PagedSource src;
-  long long q_stride_seq, q_stride_head, q_stride_token;
-  long long o_stride_seq, o_stride_head, o_stride_token;
-  int num_seqs, group, packed, max_query_len, index64;
-  int table_width;
-  int sw_mask;
-  float scale_log2;
-};
 
 template <int D>
 struct PrefillShape : KvTileShape<D> {
@@ -367,6 +351,35 @@ int launch_paged_prefill(const b200_cache_desc* c, const b200_prefill_args* a, c
   p.table_width = a->table_width;
   p.sw_mask = geo.swizzle_bytes == 0 ? 0 : geo.swizzle_bytes / 16 - 1;
   p.scale_log2 = a->scale * 1.4426950408889634f;
+
+  if (a->kernel != B200_PREFILL_AUTO && a->kernel != B200_PREFILL_TCGEN05 &&
+      a->kernel != B200_PREFILL_MMA_SYNC)
+    return set_error(B200_ERR_INVALID, "unknown prefill kernel selector");
+  // tcgen05 kernel: head_dim 64/128, 128-byte swizzled cache tiles, 16-byte
+  // aligned query/output rows (it moves rows with 16-byte vectors).
+  const long long row_bits = a->q_stride_head | a->q_stride_token | a->o_stride_head |
+                             a->o_stride_token |
+                             (a->query_layout == 0 ? (a->q_stride_seq | a->o_stride_seq) : 0);
+  const bool tc_ok = (c->head_dim == 64 || c->head_dim == 128) && geo.swizzle_bytes == 128 &&
+                     geo.chunk_bytes == 128 && (row_bits & 7) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  if (a->kernel == B200_PREFILL_TCGEN05 && !tc_ok)
+    return set_error(B200_ERR_UNSUPPORTED,
+                     "tcgen05 prefill needs head_dim 64/128, block_size >= 8 and 16-byte aligned "
+                     "query/output rows");
+  if (tc_ok && a->kernel != B200_PREFILL_MMA_SYNC) {
+    long long tx;
+    if (a->query_layout == 0) {
+      tx = static_cast<long long>(a->num_seqs) * ((a->max_query_len + kTcRows - 1) / kTcRows);
+    } else {
+      if (a->total_query_tokens <= 0) return B200_OK;
+      tx = (a->total_query_tokens + kTcRows - 1) / kTcRows + a->num_seqs;
+    }
+    if (tx > 0x7fffffffLL) return set_error(B200_ERR_UNSUPPORTED, "prefill grid too large");
+    return launch_prefill_tc(kmap, vmap, p, c->head_dim, c->dtype == B200_BF16,
+                             static_cast<unsigned>(tx), static_cast<unsigned>(a->num_q_heads),
+                             stream);
+  }
 
   long long gx;
   if (a->query_layout == 0) {

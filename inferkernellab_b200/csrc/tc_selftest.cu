@@ -1,0 +1,128 @@
+// Self-test of the tcgen05 building blocks the prefill kernel relies on: the
+// SW128 K-major and MN-major shared-memory descriptors, kind::f16 MMAs into
+// TMEM with K stepping, commit to an mbarrier, and tcgen05.ld readback.
+//
+//   C1[128, 64]  = A[128, 64] . B[64, 64]^T      (A, B K-major)
+//   C2[128, 128] = A[128, 64] . V[64, 128]        (V row-major = MN-major B)
+//
+// Operands are written to shared memory by threads with the 128-byte swizzle
+// pattern TMA produces.  One CTA of 128 threads.
+#include "../../include/b200_paged_attn.h"
+#include "common.cuh"
+#include "host_common.h"
+#include "tcgen05.cuh"
+
+namespace b200 {
+
+namespace {
+
+template <typename E>
+__global__ void __launch_bounds__(128) tc_selftest_kernel(const uint16_t* a, const uint16_t* b,
+                                                          const uint16_t* v, float* c1, float* c2,
+                                                          uint32_t* err) {
+  __shared__ __align__(1024) uint8_t sa[128 * 128];
+  __shared__ __align__(1024) uint8_t sb[64 * 128];
+  __shared__ __align__(1024) uint8_t sv[2 * 64 * 128];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+
+  // Operands -> shared memory, swizzled.
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(a + tid * 64);
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(sa + tc::sw128_offset(tid, c)) = src[c];
+  }
+  if (tid < 64) {
+    const uint4* src = reinterpret_cast<const uint4*>(b + tid * 64);
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(sb + tc::sw128_offset(tid, c)) = src[c];
+    const uint4* vs = reinterpret_cast<const uint4*>(v + tid * 128);  // K row `tid`
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      *reinterpret_cast<uint4*>(sv + tc::sw128_offset(tid, c)) = vs[c];
+      *reinterpret_cast<uint4*>(sv + 8192 + tc::sw128_offset(tid, c)) = vs[8 + c];
+    }
+  }
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  tc::fence_proxy_async_smem();
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_base, 256);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = tmem_base;
+
+  if (tid == 0) {
+    const bool bf16 = E::kIsBf16;
+    const uint32_t a0 = smem_u32(sa), b0 = smem_u32(sb), v0 = smem_u32(sv);
+    const uint32_t id1 = tc::idesc_f16(128, 64, bf16, false, false);
+    const uint32_t id2 = tc::idesc_f16(128, 128, bf16, false, true);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      tc::mma_f16(tbase, tc::sdesc_sw128(a0 + 32 * k, 16, 1024),
+                  tc::sdesc_sw128(b0 + 32 * k, 16, 1024), id1, k > 0);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      tc::mma_f16(tbase + 128, tc::sdesc_sw128(a0 + 32 * k, 16, 1024),
+                  tc::sdesc_sw128(v0 + 2048 * k, 8192, 1024), id2, k > 0);
+    tc::commit(&bar);
+  }
+  const bool ok = mbar_wait_bounded(&bar, 0, reinterpret_cast<volatile int*>(&abort_flag), err,
+                                    kErrWaitFull);
+  tc::fence_after_sync();
+  if (ok) {
+    const int row = warp * 32 + (tid & 31);
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(warp * 32) << 16);
+    uint32_t r[32];
+#pragma unroll
+    for (int cb = 0; cb < 2; ++cb) {
+      tc::ld32(lane_addr + cb * 32, r);
+      tc::wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) c1[row * 64 + cb * 32 + j] = __uint_as_float(r[j]);
+    }
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+      tc::ld32(lane_addr + 128 + cb * 32, r);
+      tc::wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) c2[row * 128 + cb * 32 + j] = __uint_as_float(r[j]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tbase, 256);
+}
+
+}  // namespace
+
+int launch_tc_selftest(const void* a, const void* b, const void* v, float* c1, float* c2,
+                       int32_t dtype, uint32_t* err, cudaStream_t stream) {
+  if (!a || !b || !v || !c1 || !c2) return set_error(B200_ERR_INVALID, "null pointer");
+  if (((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+        reinterpret_cast<uintptr_t>(v)) & 15) != 0)
+    return set_error(B200_ERR_INVALID, "operands must be 16-byte aligned");
+  const uint16_t* pa = static_cast<const uint16_t*>(a);
+  const uint16_t* pb = static_cast<const uint16_t*>(b);
+  const uint16_t* pv = static_cast<const uint16_t*>(v);
+  if (dtype == B200_BF16)
+    tc_selftest_kernel<BF16><<<1, 128, 0, stream>>>(pa, pb, pv, c1, c2, err);
+  else if (dtype == B200_F16)
+    tc_selftest_kernel<Half><<<1, 128, 0, stream>>>(pa, pb, pv, c1, c2, err);
+  else
+    return set_error(B200_ERR_UNSUPPORTED, "dtype must be float16 or bfloat16");
+  return cuda_status(cudaGetLastError(), "tc_selftest_kernel launch");
+}
+
+}  // namespace b200

@@ -1,0 +1,143 @@
+// Blackwell (sm_100a) 5th-generation tensor-core helpers: tcgen05.mma with
+// shared-memory operand descriptors, tensor memory (TMEM) allocation, loads and
+// stores, commit-to-mbarrier and the tcgen05 ordering fences.  Inline PTX only.
+//
+// Operand layouts used here (both produced by TMA with 128-byte swizzle or
+// written by threads with the same XOR pattern):
+//   K-major, SW128:  rows of 64 16-bit elements (128 bytes) along K, row r at
+//                    byte r*128 of a 1024-byte aligned region, 16-byte chunk c
+//                    stored at chunk position c ^ (r & 7).  Stride between
+//                    8-row groups (SBO) = 1024 bytes.  One MMA consumes 16
+//                    elements of K: advance the start address by 32 bytes.
+//   MN-major, SW128: the same physical rows, but a row holds 64 elements along
+//                    M/N and successive rows are successive K.  SBO = 1024
+//                    bytes (8 K-rows), LBO = byte distance between 64-element
+//                    groups of M/N.  One MMA consumes 16 K-rows: advance the
+//                    start address by 2048 bytes.
+// Encodings follow the sm_100 UMMA descriptor definitions (shared-memory
+// descriptor: start>>4 at [0,14), LBO>>4 at [16,30), SBO>>4 at [32,46),
+// version 1 at [46,48), layout type at [61,64) with 2 = 128-byte swizzle;
+// instruction descriptor: D format at [4,6), A/B formats at [7,10)/[10,13),
+// A/B major at bits 15/16, N>>3 at [17,23), M>>4 at [24,29)).
+#pragma once
+
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace b200 {
+namespace tc {
+
+// Instruction descriptor of kind::f16 with an fp32 accumulator.
+// bf16: true for bfloat16 operands, false for float16 (A and B always agree).
+// a_mn / b_mn: operand is MN-major (true) or K-major (false).
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool bf16, bool a_mn, bool b_mn) {
+  return (1u << 4)                                           // D = f32
+         | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10)  // A, B formats
+         | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16)  // majors
+         | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3fffu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3fffu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3fffu) << 32;
+  d |= 1ull << 46;  // descriptor version for sm_100
+  d |= 2ull << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// ---------------------------------------------------------------- TMEM
+// Allocation is warp-wide; the TMEM base address is written to `dst` (shared).
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Generic-proxy shared-memory writes -> visible to the async proxy (MMA, TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
+// Arrive (once) on `bar` when every tcgen05 operation this thread issued so
+// far has completed.
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// Warp-collective: lane i of warp w (w = warp index % 4) reads 32 consecutive
+// 32-bit columns of TMEM lane 32*w + i starting at `taddr` (lane field = 32*w).
+__device__ __forceinline__ void ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 128-byte
+// swizzled region (1024-byte aligned base).
+__device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
+  return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+}  // namespace tc
+}  // namespace b200

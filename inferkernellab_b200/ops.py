@@ -33,6 +33,9 @@ import torch
 from . import _lib
 
 _DTYPE_CODE = {torch.float16: _lib.B200_F16, torch.bfloat16: _lib.B200_BF16}
+# Prefill kernel selector: "auto" takes the tcgen05/TMEM kernel where it applies
+# (head_dim 64/128, block_size >= 8), else the mma.sync kernel.
+_PREFILL_KERNEL = {"auto": 0, "tcgen05": 1, "mma_sync": 2}
 _INDEX_CODE = {torch.int32: _lib.B200_I32, torch.int64: _lib.B200_I64}
 
 
@@ -437,8 +440,14 @@ def _prefill_index(values, device) -> tuple[torch.Tensor, list[int]]:
     return torch.tensor(host, dtype=torch.int64, device=device), host
 
 
+def _prefill_kernel(kernel: str) -> int:
+    if kernel not in _PREFILL_KERNEL:
+        raise ValueError(f"kernel must be one of {sorted(_PREFILL_KERNEL)}")
+    return _PREFILL_KERNEL[kernel]
+
+
 def paged_prefill_attention(query: torch.Tensor, cache, block_tables, query_starts, context_lens,
-                            *, scale=None, layer: int = 0) -> torch.Tensor:
+                            *, scale=None, layer: int = 0, kernel: str = "auto") -> torch.Tensor:
     """Ragged causal prefill over the paged cache, padded ``[B, Hq, T, D]`` form.
 
     Drop-in for ``paged_prefill_attention_sdpa`` (reference ``attention.py:230-321``):
@@ -489,7 +498,7 @@ def paged_prefill_attention(query: torch.Tensor, cache, block_tables, query_star
         query.stride(0), query.stride(1), query.stride(2),
         out.stride(0), out.stride(1), out.stride(2), tables.stride(0),
         _INDEX_CODE[tables.dtype], _lib.B200_I64,
-        float(scale) if scale is not None else head_dim ** -0.5)
+        float(scale) if scale is not None else head_dim ** -0.5, _prefill_kernel(kernel))
     _lib.check(_lib.load().b200_paged_prefill(
         ctypes.byref(desc), ctypes.byref(args), query.data_ptr(), tables.data_ptr(),
         starts_t.data_ptr(), ends_t.data_ptr(), None, out.data_ptr(),
@@ -500,7 +509,8 @@ def paged_prefill_attention(query: torch.Tensor, cache, block_tables, query_star
 def paged_prefill_attention_varlen(query: torch.Tensor, cache, block_tables: torch.Tensor,
                                    cu_seqlens_q: torch.Tensor, query_starts: torch.Tensor,
                                    context_lens: torch.Tensor, *, scale=None, layer: int = 0,
-                                   out: torch.Tensor | None = None) -> torch.Tensor:
+                                   out: torch.Tensor | None = None,
+                                   kernel: str = "auto") -> torch.Tensor:
     """Packed ragged causal prefill: ``query`` ``[sum T, Hq, D]``, no padding.
 
     Sequence ``b`` owns rows ``cu_seqlens_q[b] .. cu_seqlens_q[b+1]-1`` which
@@ -541,7 +551,7 @@ def paged_prefill_attention_varlen(query: torch.Tensor, cache, block_tables: tor
         batch, num_heads, block_tables.shape[1], layer, 1, 0, total,
         0, query.stride(1), query.stride(0), 0, out.stride(1), out.stride(0),
         block_tables.stride(0), _INDEX_CODE[block_tables.dtype], _INDEX_CODE[query_starts.dtype],
-        float(scale) if scale is not None else head_dim ** -0.5)
+        float(scale) if scale is not None else head_dim ** -0.5, _prefill_kernel(kernel))
     _lib.check(_lib.load().b200_paged_prefill(
         ctypes.byref(desc), ctypes.byref(args), query.data_ptr(), block_tables.data_ptr(),
         query_starts.contiguous().data_ptr(), context_lens.contiguous().data_ptr(),
