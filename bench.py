@@ -325,7 +325,7 @@ def run_ours(args, world, rank, local) -> dict | None:
         "decode_tok_s": round(wl.batch * world * k_steps / (elapsed_ms * 1e-3), 1),
         "roofline": {
             "bound": "hbm",
-            "kernel": "paged_decode_kernel<BF16,128,1>",
+            "kernel": "paged_decode_kernel<BF16,128,-1> (G=4: keys as M, group as N)",
             "achieved": round(achieved, 2),
             "peak": peak,
             "unit": "GB/s",
