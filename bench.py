@@ -8,9 +8,13 @@ physical pool = total blocks + 10 %, shuffled allocation.  One *step* is one
 decode step of the hot path for the batch:
 
   1. append the new token's K/V of every request through its slot
-     (``append_kv``, reshape-and-cache), then
-  2. paged decode attention of every request over its whole context
-     (``paged_decode_attention``), context length = drawn length.
+     (reshape-and-cache), and
+  2. paged decode attention of every request over its whole context,
+     context length = drawn length (the new token is the last position),
+
+both in one launch: ``paged_decode_attention_append`` (the attention kernel's
+producer warp writes each new token just before it loads the tile that holds
+it; bit-identical to ``append_kv`` followed by ``paged_decode_attention``).
 
 The step is idempotent (the same slots are rewritten), so K timed steps are
 K identical passes over a 1.08 GB working set -- far larger than the 126 MB
@@ -21,7 +25,7 @@ the attention, plus the append's read and write) x steps x GPUs / the max over
 ranks of the device time of the K steps.  ``e2e`` repeats the measurement
 through the same public API with every step's inputs copied from pinned host
 memory and the output copied back inside the timed region.  ``roofline`` is the
-decode kernel alone, timed with CUDA events around each of its launches.
+step's kernel, timed with CUDA events around each of its launches.
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 numpy restatement in ``oracle/`` of the reference's ``paged_decode_attention``)
@@ -108,11 +112,10 @@ class Workload:
         return 2 * 2 * self.batch * self.num_kv_heads * self.head_dim * 2 + self.batch * 4
 
     def step(self):
-        from inferkernellab_b200 import append_kv, paged_decode_attention
+        from inferkernellab_b200 import paged_decode_attention_append
 
-        append_kv(self.new_k, self.new_v, self.cache, self.slots)
-        paged_decode_attention(self.query, self.cache, self.tables, self.lens,
-                               validate_inputs=False, out=self.out)
+        paged_decode_attention_append(self.query, self.new_k, self.new_v, self.cache,
+                                      self.tables, self.lens, self.slots, out=self.out)
 
 
 # ---------------------------------------------------------------- clocks
@@ -229,7 +232,7 @@ def run_ours(args, world, rank, local) -> dict | None:
     stream = torch.cuda.current_stream(device)
     for _ in range(args.warmup):
         wl.step()
-    from inferkernellab_b200 import append_kv, check_device_errors, paged_decode_attention
+    from inferkernellab_b200 import check_device_errors, paged_decode_attention_append
 
     if check_device_errors() & ~8:
         raise RuntimeError("device error word set during warm-up")
@@ -244,10 +247,9 @@ def run_ours(args, world, rank, local) -> dict | None:
         _barrier_sync(world)
         t0.record(stream)
         for i in range(k_steps):
-            append_kv(wl.new_k, wl.new_v, wl.cache, wl.slots)
             dec_start[i].record(stream)
-            paged_decode_attention(wl.query, wl.cache, wl.tables, wl.lens, validate_inputs=False,
-                                   out=wl.out)
+            paged_decode_attention_append(wl.query, wl.new_k, wl.new_v, wl.cache, wl.tables,
+                                          wl.lens, wl.slots, out=wl.out)
             dec_end[i].record(stream)
         t1.record(stream)
         _barrier_sync(world)
@@ -274,8 +276,7 @@ def run_ours(args, world, rank, local) -> dict | None:
         d_tab.copy_(tab_h, non_blocking=True)
         d_len.copy_(len_h, non_blocking=True)
         d_slot.copy_(slot_h, non_blocking=True)
-        append_kv(d_k, d_v, wl.cache, d_slot)
-        paged_decode_attention(d_q, wl.cache, d_tab, d_len, validate_inputs=False, out=d_out)
+        paged_decode_attention_append(d_q, d_k, d_v, wl.cache, d_tab, d_len, d_slot, out=d_out)
         out_h.copy_(d_out, non_blocking=True)
 
     for _ in range(3):
@@ -295,7 +296,7 @@ def run_ours(args, world, rank, local) -> dict | None:
     if rank != 0:
         return None
     peak, peak_kind = _peaks()
-    achieved = wl.decode_bytes() / (dec_ms * 1e-3) / 1e9
+    achieved = step_bytes / (dec_ms * 1e-3) / 1e9
     total_bytes = step_bytes * k_steps * world
     value = total_bytes / (elapsed_ms * 1e-3) / 1e9
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
@@ -325,7 +326,7 @@ def run_ours(args, world, rank, local) -> dict | None:
         "decode_tok_s": round(wl.batch * world * k_steps / (elapsed_ms * 1e-3), 1),
         "roofline": {
             "bound": "hbm",
-            "kernel": "paged_decode_kernel<BF16,128,-1> (G=4: keys as M, group as N)",
+            "kernel": "paged_decode_kernel<BF16,128,-1,true> (append fused; G=4: keys as M)",
             "achieved": round(achieved, 2),
             "peak": peak,
             "unit": "GB/s",
@@ -333,7 +334,7 @@ def run_ours(args, world, rank, local) -> dict | None:
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
             else "fallback 6650 GB/s",
             "traffic": _ncu_traffic(),
-            "algorithmic_bytes_per_launch": wl.decode_bytes(),
+            "algorithmic_bytes_per_launch": step_bytes,
             "avg_launch_ms": round(dec_ms, 5),
             "frac_of_nominal_8TBs": round(achieved / 8000.0, 4),
         },
@@ -343,9 +344,9 @@ def run_ours(args, world, rank, local) -> dict | None:
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
             "ms_per_step": round(e2e_ms / k_steps, 5),
-            "api": "inferkernellab_b200.append_kv + paged_decode_attention, pinned host buffers",
+            "api": "inferkernellab_b200.paged_decode_attention_append, pinned host buffers",
         },
-        "gpu_launches": 2 * k_steps,
+        "gpu_launches": k_steps,
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:

@@ -157,6 +157,34 @@ B200_API int b200_append_kv(const b200_cache_desc* cache, int32_t layer, const v
                    int64_t value_stride_token, int64_t value_stride_head, const void* slots,
                    int32_t slots_dtype, uint32_t* error_word, void* stream);
 
+/* -------------------------------------------- decode with fused append
+ * b200_paged_decode_append = b200_rope_append_kv (rope = 1) or b200_append_kv
+ * (rope = 0) of every request's new token followed by b200_paged_decode, in one
+ * launch (reference: hf_benchmark.py:69-85 rotary, append.py:69-106 append,
+ * triton_ops.py:404-478 decode).  The new token of request b must be its last
+ * context position, context_lens[b] - 1 (a decode step).  query is the
+ * un-rotated query when rope = 1; key/value [B, Hkv, D] (strides below); cos/sin
+ * [B, D] rows of the rotary table for each request's new position (rope = 1);
+ * key/value/cos/sin rows 16-byte aligned; slots [B] (negative = skip the
+ * append).  The cache holds
+ * exactly what the separate calls would write; the output matches
+ * b200_paged_decode on the rotated query.  Workspace as b200_paged_decode.
+ */
+typedef struct {
+  int32_t rope;        /* 1 = rotary embedding on query and the new key, 0 = plain append */
+  int32_t slots_dtype; /* B200_I32 / B200_I64 */
+  int64_t k_stride_seq, k_stride_head; /* elements */
+  int64_t v_stride_seq, v_stride_head;
+  int64_t cos_stride_seq, sin_stride_seq;
+} b200_decode_append_args;
+
+B200_API int b200_paged_decode_append(const b200_cache_desc* cache, const b200_decode_args* args,
+                                      const b200_decode_append_args* append, const void* query,
+                                      const void* key, const void* value, const void* cos,
+                                      const void* sin, const void* slots, const void* block_tables,
+                                      const void* context_lens, void* out, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------- fused rotary + append
  * For every token t and head h (rotate_half(x) = concat(-x[D/2:], x[:D/2])):
  *   query_out[t, h]            = query[t, h] * cos[t] + rotate_half(query[t, h]) * sin[t]

@@ -6,6 +6,8 @@ operators plus host mirrors of its cache, scheduler and runtime:
 * ``paged_decode_attention`` -- split-KV paged decode (MHA/GQA/MQA);
 * ``append_kv`` -- reshape-and-cache through ``slot_mapping``, bit-exact;
 * ``rope_append_kv`` -- rotary embedding of q/k fused with the K/V append;
+* ``paged_decode_attention_append`` -- a decode step's append (+ rotary) fused
+  into the attention launch;
 * ``paged_prefill_attention`` / ``paged_prefill_attention_varlen`` -- ragged
   causal prefill over the paged cache;
 * ``build_slot_mapping`` -- device-built slots + ``cu_seqlens`` for a batch;
@@ -26,6 +28,7 @@ from .ops import (
     build_slot_mapping,
     check_device_errors,
     paged_decode_attention,
+    paged_decode_attention_append,
     paged_prefill_attention,
     paged_prefill_attention_varlen,
     rope_append_kv,
@@ -60,6 +63,7 @@ __all__ = [
     "build_slot_mapping",
     "check_device_errors",
     "paged_decode_attention",
+    "paged_decode_attention_append",
     "paged_decode_attention_b200",
     "paged_prefill_attention",
     "paged_prefill_attention_b200",

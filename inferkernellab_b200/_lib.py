@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "b200_paged_decode_noalloc_scratch_bytes",
     "b200_append_kv",
     "b200_rope_append_kv",
+    "b200_paged_decode_append",
     "b200_add_rmsnorm",
     "b200_silu_mul",
     "b200_tc_selftest",
@@ -106,6 +107,19 @@ class PrefillArgs(ctypes.Structure):
     ]
 
 
+class DecodeAppendArgs(ctypes.Structure):
+    _fields_ = [
+        ("rope", ctypes.c_int32),
+        ("slots_dtype", ctypes.c_int32),
+        ("k_stride_seq", ctypes.c_int64),
+        ("k_stride_head", ctypes.c_int64),
+        ("v_stride_seq", ctypes.c_int64),
+        ("v_stride_head", ctypes.c_int64),
+        ("cos_stride_seq", ctypes.c_int64),
+        ("sin_stride_seq", ctypes.c_int64),
+    ]
+
+
 class RopeAppendArgs(ctypes.Structure):
     _fields_ = [
         ("num_tokens", ctypes.c_int64),
@@ -139,6 +153,11 @@ _PROTOTYPES = {
     "b200_paged_decode_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "b200_append_kv": (ctypes.c_int, [ctypes.POINTER(CacheDesc), _i32, _vp, _vp, _i64, _i64, _i64,
                                       _i64, _i64, _vp, _i32, _vp, _vp]),
+    "b200_paged_decode_append": (ctypes.c_int, [ctypes.POINTER(CacheDesc),
+                                                ctypes.POINTER(DecodeArgs),
+                                                ctypes.POINTER(DecodeAppendArgs), _vp, _vp, _vp,
+                                                _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t,
+                                                _vp]),
     "b200_rope_append_kv": (ctypes.c_int, [ctypes.POINTER(CacheDesc),
                                            ctypes.POINTER(RopeAppendArgs), _vp, _vp, _vp, _vp,
                                            _vp, _vp, _vp, _vp, _vp]),

@@ -81,6 +81,18 @@ int b200_append_kv(const b200_cache_desc* cache, int32_t layer, const void* key,
   });
 }
 
+int b200_paged_decode_append(const b200_cache_desc* cache, const b200_decode_args* args,
+                             const b200_decode_append_args* append, const void* query,
+                             const void* key, const void* value, const void* cos, const void* sin,
+                             const void* slots, const void* block_tables, const void* context_lens,
+                             void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  return guarded([&] {
+    return b200::launch_paged_decode_append(cache, args, append, query, key, value, cos, sin,
+                                            slots, block_tables, context_lens, out, workspace,
+                                            workspace_bytes, as_stream(stream));
+  });
+}
+
 int b200_rope_append_kv(const b200_cache_desc* cache, const b200_rope_append_args* args,
                         const void* query, const void* key, const void* value, const void* cos,
                         const void* sin, const void* slots, void* query_out,

@@ -205,6 +205,35 @@ __device__ __forceinline__ __nv_bfloat16 from_float<BF16>(float x) {
   return __float2bfloat16_rn(x);
 }
 
+template <typename E>
+__device__ __forceinline__ float to_float(typename E::T x);
+template <>
+__device__ __forceinline__ float to_float<Half>(__half x) {
+  return __half2float(x);
+}
+template <>
+__device__ __forceinline__ float to_float<BF16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+// Round to the 16-bit type and widen back: what one torch elementwise op on
+// 16-bit tensors stores.
+template <typename E>
+__device__ __forceinline__ float round_to(float x) {
+  return to_float<E>(from_float<E>(x));
+}
+
+// Rotary embedding of one pair (a = x[i], b = x[i + D/2]) with the rounding of
+// the reference's torch elementwise form x*cos + rotate_half(x)*sin
+// (hf_benchmark.py:69-85): each product rounded, the sum rounded by the caller's
+// final conversion.  c_lo/s_lo are cos/sin at i, c_hi/s_hi at i + D/2.
+template <typename E>
+__device__ __forceinline__ void rope_pair(float a, float b, float c_lo, float s_lo, float c_hi,
+                                          float s_hi, float& lo, float& hi) {
+  lo = round_to<E>(a * c_lo) + round_to<E>(-b * s_lo);
+  hi = round_to<E>(b * c_hi) + round_to<E>(a * s_hi);
+}
+
 // Hardware base-2 exponential (PTX ex2.approx.ftz.f32); ex2(-inf) = +0.
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

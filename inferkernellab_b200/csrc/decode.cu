@@ -61,6 +61,22 @@ struct DecodeParams {
   int box_rows, sw_mask;
   int table64, lens64;
   float scale_log2;
+  // Fused new-token append (b200_paged_decode_append); fuse_append == 0 = off.
+  // The new token of request r is its last context position (lens[r] - 1): the
+  // CTA that owns the tile holding that position writes its K (rotated when
+  // rope) and V at new_slots[r] before its first TMA load; with rope the
+  // consumers rotate q.
+  int fuse_append, rope, slots64;
+  const void* new_k;
+  const void* new_v;
+  const void* cos;
+  const void* sin;
+  const void* new_slots;
+  void* k_cache;
+  void* v_cache;
+  long long nk_stride_seq, nk_stride_head, nv_stride_seq, nv_stride_head;
+  long long cos_stride, sin_stride;
+  long long slots_per_layer;
 };
 
 // Ring depth per CTA and CTAs per SM (kDecMinBlocks feeds __launch_bounds__).
@@ -151,6 +167,154 @@ struct TileCursor {
   }
 };
 
+// All threads of the CTA, before any TMA load: write the new token (position
+// len - 1) of every segment whose last tile lies in [my_begin, my_end).  Only
+// this CTA loads that tile, so no other CTA can read the token's cache row.  K
+// is rotated with the reference's rounding when p.rope, V is copied; 16-byte
+// vectors (the host checks the alignment).  Each thread loads all it needs for
+// an item before it stores, so one item costs one memory round trip.
+template <typename E, int D>
+__device__ __forceinline__ void append_range_tokens(const DecodeParams& p, const int* begin_s,
+                                                    const int* len_s, int my_begin, int my_end) {
+  using T = typename E::T;
+  constexpr int kVec = D / 8;         // 16-byte vectors per cache row
+  constexpr int kItems = 2 * kVec;    // V vectors, then K vectors (rope: K vector pairs)
+  const int hkv = p.num_kv_heads;
+  TileCursor first, last;
+  first.init(my_begin, begin_s, len_s, p.num_seqs, hkv);
+  last.init(my_end - 1, begin_s, len_s, p.num_seqs, hkv);
+  const int g0 = first.r * hkv + first.h;
+  const int nseg = last.r * hkv + last.h - g0 + 1;
+  for (int it = threadIdx.x; it < nseg * kItems; it += blockDim.x) {
+    const int k = it / kItems;
+    const int item = it - k * kItems;
+    const int g = g0 + k;
+    const int r = g / hkv;
+    const int h = g - r * hkv;
+    const int len = len_s[r];
+    if (len == 0) continue;
+    const int nt = (len + kDecTile - 1) / kDecTile;
+    const int last_tile = begin_s[r] + h * nt + nt - 1;
+    if (last_tile < my_begin || last_tile >= my_end) continue;
+    const long long slot = load_index(p.new_slots, r, p.slots64);
+    if (slot < 0) continue;  // padding slot: nothing to append
+    if (slot >= p.slots_per_layer) {
+      if (item == 0 && p.err) atomicOr(p.err, kErrBadSlot);
+      continue;
+    }
+    const long long row = ((p.layer_slot_base + slot) * hkv + h) * D;
+    if (item < kVec) {
+      const uint4* vs = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.new_v) +
+                                                       r * p.nv_stride_seq + h * p.nv_stride_head);
+      reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.v_cache) + row)[item] = vs[item];
+      continue;
+    }
+    const int j = item - kVec;
+    const uint4* ks = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.new_k) +
+                                                     r * p.nk_stride_seq + h * p.nk_stride_head);
+    uint4* kd = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.k_cache) + row);
+    if (!p.rope) {
+      kd[j] = ks[j];
+      continue;
+    }
+    if (j >= kVec / 2) continue;  // the pair (j, j + D/16) is handled by item j
+    const uint4* cv = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.cos) +
+                                                     r * p.cos_stride);
+    const uint4* sv = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.sin) +
+                                                     r * p.sin_stride);
+    const uint4 a4 = ks[j], b4 = ks[j + kVec / 2];
+    const uint4 cl4 = cv[j], ch4 = cv[j + kVec / 2], sl4 = sv[j], sh4 = sv[j + kVec / 2];
+    const T* a = reinterpret_cast<const T*>(&a4);
+    const T* b = reinterpret_cast<const T*>(&b4);
+    const T* cl = reinterpret_cast<const T*>(&cl4);
+    const T* ch = reinterpret_cast<const T*>(&ch4);
+    const T* sl = reinterpret_cast<const T*>(&sl4);
+    const T* sh = reinterpret_cast<const T*>(&sh4);
+    uint4 lo4, hi4;
+    T* lo = reinterpret_cast<T*>(&lo4);
+    T* hi = reinterpret_cast<T*>(&hi4);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float l, u;
+      rope_pair<E>(to_float<E>(a[e]), to_float<E>(b[e]), to_float<E>(cl[e]), to_float<E>(sl[e]),
+                   to_float<E>(ch[e]), to_float<E>(sh[e]), l, u);
+      lo[e] = from_float<E>(l);
+      hi[e] = from_float<E>(u);
+    }
+    kd[j] = lo4;
+    kd[j + kVec / 2] = hi4;
+  }
+}
+
+// Rotate one pair of fragment registers: `lo` holds q[d], q[d+1] and `hi` holds
+// q[d+D/2], q[d+D/2+1] of the same head (the two halves of a rotary pair always
+// land in the same thread of an m16n8k16 fragment).
+template <typename E>
+__device__ __forceinline__ void rope_frag_pair(uint32_t& lo, uint32_t& hi, const typename E::T* c,
+                                               const typename E::T* sn, int d, int half) {
+  using T = typename E::T;
+  const uint32_t cl = *reinterpret_cast<const uint32_t*>(c + d);
+  const uint32_t ch = *reinterpret_cast<const uint32_t*>(c + d + half);
+  const uint32_t sl = *reinterpret_cast<const uint32_t*>(sn + d);
+  const uint32_t sh = *reinterpret_cast<const uint32_t*>(sn + d + half);
+  auto elem = [](uint32_t v, int e) {
+    const uint16_t bits = static_cast<uint16_t>(e ? v >> 16 : v & 0xffffu);
+    T t;
+    memcpy(&t, &bits, 2);
+    return to_float<E>(t);
+  };
+  float l0, h0, l1, h1;
+  rope_pair<E>(elem(lo, 0), elem(hi, 0), elem(cl, 0), elem(sl, 0), elem(ch, 0), elem(sh, 0), l0,
+               h0);
+  rope_pair<E>(elem(lo, 1), elem(hi, 1), elem(cl, 1), elem(sl, 1), elem(ch, 1), elem(sh, 1), l1,
+               h1);
+  lo = pack2<E>(l0, l1);
+  hi = pack2<E>(h0, h1);
+}
+
+// Rotary embedding of the query fragments of one segment.  Register (kk, j)
+// holds dims d = 16*kk + 8*j + 2*tq (+1); its partner d + D/2 is register
+// (kk + D/32, j) for D >= 32 and (kk, 1) for D = 16.
+template <typename E, int D, int NT>
+__device__ __forceinline__ void rope_qT_frag(uint32_t (&qb)[NT][D / 16][2],
+                                             const typename E::T* c, const typename E::T* sn,
+                                             int lane) {
+  const int tq = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    if constexpr (D >= 32) {
+#pragma unroll
+      for (int kk = 0; kk < D / 32; ++kk)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          rope_frag_pair<E>(qb[nt][kk][j], qb[nt][kk + D / 32][j], c, sn, 16 * kk + 8 * j + 2 * tq,
+                            D / 2);
+    } else {
+      rope_frag_pair<E>(qb[nt][0][0], qb[nt][0][1], c, sn, 2 * tq, D / 2);
+    }
+  }
+}
+
+// Same for the heads-as-M A fragments: qf[kk][0|2] = row g, qf[kk][1|3] = row g + 8.
+template <typename E, int D>
+__device__ __forceinline__ void rope_q_frag(uint32_t (&qf)[D / 16][4], const typename E::T* c,
+                                            const typename E::T* sn, int lane) {
+  const int tq = lane & 3;
+#pragma unroll
+  for (int row = 0; row < 2; ++row) {
+    if constexpr (D >= 32) {
+#pragma unroll
+      for (int kk = 0; kk < D / 32; ++kk)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          rope_frag_pair<E>(qf[kk][2 * j + row], qf[kk + D / 32][2 * j + row], c, sn,
+                            16 * kk + 8 * j + 2 * tq, D / 2);
+    } else {
+      rope_frag_pair<E>(qf[0][row], qf[0][2 + row], c, sn, 2 * tq, D / 2);
+    }
+  }
+}
+
 __device__ __forceinline__ float fast_log2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -180,7 +344,9 @@ __device__ __forceinline__ void store4(typename E::T* dst, float4 v) {
 
 constexpr int kMinTilesPerCta = 2;  // fewer split pieces on small problems
 
-template <typename E, int D, int MT>
+// FUSED: the new-token append (and rotary embedding) of b200_paged_decode_append
+// is compiled in; the plain decode instantiation carries none of that code.
+template <typename E, int D, int MT, bool FUSED>
 __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
@@ -287,6 +453,12 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   const int my_end = min(total, my_begin + per_cta);
   const int n_tiles = my_end - my_begin;
   if (n_tiles <= 0) return;
+  if constexpr (FUSED) {
+    append_range_tokens<E, D>(p, begin_s, len_s, my_begin, my_end);
+    // Generic-proxy cache writes -> visible to this CTA's TMA loads.
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncthreads();
+  }
 
   const uint32_t smem_base = smem_u32(smem);
 
@@ -359,6 +531,9 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
                     static_cast<long long>(cur.h * G) * p.q_stride_head;
       if constexpr (kTrans) {
         load_qT_frag<E, D, NT>(qb, qg, p.q_stride_head, G, lane);
+        if (FUSED && p.rope)
+          rope_qT_frag<E, D, NT>(qb, reinterpret_cast<const T*>(p.cos) + cur.r * p.cos_stride,
+                                 reinterpret_cast<const T*>(p.sin) + cur.r * p.sin_stride, lane);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -369,6 +544,9 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       } else {
         load_q_frag<E, D>(qf, row0 < G ? qg + row0 * p.q_stride_head : nullptr,
                           row1 < G ? qg + row1 * p.q_stride_head : nullptr, tq);
+        if (FUSED && p.rope)
+          rope_q_frag<E, D>(qf, reinterpret_cast<const T*>(p.cos) + cur.r * p.cos_stride,
+                            reinterpret_cast<const T*>(p.sin) + cur.r * p.sin_stride, lane);
 #pragma unroll
         for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
         m_r[0] = m_r[1] = -INFINITY;
@@ -673,14 +851,15 @@ static int launch_decode_t(const CUtensorMap& kmap, const CUtensorMap& vmap,
                            cudaStream_t stream) {
   const DecodeSmem L = decode_smem_layout<D, MT>(p.group, p.num_seqs);
   const int smem = L.total + 1024;
-  auto kern = paged_decode_kernel<E, D, MT>;
-  static int configured_smem[64] = {0};
+  const int fused = p.fuse_append ? 1 : 0;
+  auto kern = fused ? paged_decode_kernel<E, D, MT, true> : paged_decode_kernel<E, D, MT, false>;
+  static int configured_smem[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && configured_smem[dev] < smem) {
+  if (dev < 64 && configured_smem[fused][dev] < smem) {
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (err != cudaSuccess) return cuda_status(err, "cudaFuncSetAttribute(decode smem)");
-    configured_smem[dev] = smem;
+    configured_smem[fused][dev] = smem;
   }
   int per_sm = 0;
   cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, smem);
@@ -781,11 +960,41 @@ size_t decode_workspace_bytes(const b200_cache_desc* c, const b200_decode_args* 
   return workspace_layout(a->num_seqs, c->num_kv_heads, group, c->head_dim, grid).total;
 }
 
-int launch_paged_decode(const b200_cache_desc* c, const b200_decode_args* a, const void* query,
-                        const void* block_tables, const void* context_lens, void* out,
-                        void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+// Inputs of the fused new-token append (b200_paged_decode_append).
+struct FusedAppend {
+  const b200_decode_append_args* args;
+  const void* key;
+  const void* value;
+  const void* cos;
+  const void* sin;
+  const void* slots;
+};
+
+static int launch_decode_common(const b200_cache_desc* c, const b200_decode_args* a,
+                                const void* query, const void* block_tables,
+                                const void* context_lens, void* out, void* workspace,
+                                size_t workspace_bytes, const FusedAppend* f,
+                                cudaStream_t stream) {
   int rc = check_decode_args(c, a);
   if (rc != B200_OK) return rc;
+  if (f != nullptr) {
+    const b200_decode_append_args* fa = f->args;
+    if (fa == nullptr) return set_error(B200_ERR_INVALID, "null append descriptor");
+    if (fa->rope != 0 && fa->rope != 1) return set_error(B200_ERR_INVALID, "rope must be 0 or 1");
+    if (!f->key || !f->value || !f->slots)
+      return set_error(B200_ERR_INVALID, "null key/value/slots pointer");
+    // The new rows move as 16-byte vectors.
+    if (((reinterpret_cast<uintptr_t>(f->key) | reinterpret_cast<uintptr_t>(f->value)) & 15) ||
+        ((fa->k_stride_seq | fa->k_stride_head | fa->v_stride_seq | fa->v_stride_head) & 7))
+      return set_error(B200_ERR_INVALID, "key/value rows must be 16-byte aligned");
+    if (fa->rope) {
+      if (!f->cos || !f->sin) return set_error(B200_ERR_INVALID, "rope needs cos and sin");
+      // q fragments and cos/sin are read as aligned pairs of 16-bit elements.
+      if (((reinterpret_cast<uintptr_t>(f->cos) | reinterpret_cast<uintptr_t>(f->sin)) & 15) ||
+          ((fa->cos_stride_seq | fa->sin_stride_seq) & 7))
+        return set_error(B200_ERR_INVALID, "cos/sin rows must be 16-byte aligned");
+    }
+  }
   if (!query || !block_tables || !context_lens || !out || !c->k_cache || !c->v_cache)
     return set_error(B200_ERR_INVALID, "null tensor pointer");
   if ((reinterpret_cast<uintptr_t>(query) & 3) || (reinterpret_cast<uintptr_t>(out) & 7))
@@ -826,6 +1035,25 @@ int launch_paged_decode(const b200_cache_desc* c, const b200_decode_args* a, con
   p.table64 = a->table_dtype == B200_I64;
   p.lens64 = a->lens_dtype == B200_I64;
   p.scale_log2 = a->scale * 1.4426950408889634f;
+  if (f != nullptr) {
+    p.fuse_append = 1;
+    p.rope = f->args->rope;
+    p.slots64 = f->args->slots_dtype == B200_I64;
+    p.new_k = f->key;
+    p.new_v = f->value;
+    p.cos = f->cos;
+    p.sin = f->sin;
+    p.new_slots = f->slots;
+    p.k_cache = c->k_cache;
+    p.v_cache = c->v_cache;
+    p.nk_stride_seq = f->args->k_stride_seq;
+    p.nk_stride_head = f->args->k_stride_head;
+    p.nv_stride_seq = f->args->v_stride_seq;
+    p.nv_stride_head = f->args->v_stride_head;
+    p.cos_stride = f->args->cos_stride_seq;
+    p.sin_stride = f->args->sin_stride_seq;
+    p.slots_per_layer = static_cast<long long>(c->num_blocks) * c->block_size;
+  }
 
   int grid = 0;
   rc = c->dtype == B200_BF16
@@ -846,6 +1074,24 @@ int launch_paged_decode(const b200_cache_desc* c, const b200_decode_args* a, con
   return c->dtype == B200_BF16
              ? dispatch_d<BF16>(c->head_dim, mt, kmap, vmap, p, info.num_sms, &grid, false, stream)
              : dispatch_d<Half>(c->head_dim, mt, kmap, vmap, p, info.num_sms, &grid, false, stream);
+}
+
+int launch_paged_decode(const b200_cache_desc* c, const b200_decode_args* a, const void* query,
+                        const void* block_tables, const void* context_lens, void* out,
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return launch_decode_common(c, a, query, block_tables, context_lens, out, workspace,
+                              workspace_bytes, nullptr, stream);
+}
+
+int launch_paged_decode_append(const b200_cache_desc* c, const b200_decode_args* a,
+                               const b200_decode_append_args* fa, const void* query,
+                               const void* key, const void* value, const void* cos,
+                               const void* sin, const void* slots, const void* block_tables,
+                               const void* context_lens, void* out, void* workspace,
+                               size_t workspace_bytes, cudaStream_t stream) {
+  const FusedAppend f{fa, key, value, cos, sin, slots};
+  return launch_decode_common(c, a, query, block_tables, context_lens, out, workspace,
+                              workspace_bytes, &f, stream);
 }
 
 // ------------------------------------------------------ allocation-free entry

@@ -14,6 +14,14 @@ int launch_paged_decode(const b200_cache_desc* c, const b200_decode_args* a, con
                         const void* block_tables, const void* context_lens, void* out,
                         void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+// Decode with the new token's K/V append (and rotary embedding) fused in.
+int launch_paged_decode_append(const b200_cache_desc* c, const b200_decode_args* a,
+                               const b200_decode_append_args* fa, const void* query,
+                               const void* key, const void* value, const void* cos,
+                               const void* sin, const void* slots, const void* block_tables,
+                               const void* context_lens, void* out, void* workspace,
+                               size_t workspace_bytes, cudaStream_t stream);
+
 // Allocation-free variant: split scratch from a static device array (decode.cu).
 size_t decode_noalloc_scratch_bytes();
 int launch_paged_decode_noalloc(const b200_cache_desc* c, const b200_decode_args* a,

@@ -21,22 +21,6 @@ namespace b200 {
 
 namespace {
 
-template <typename E>
-__device__ __forceinline__ float to_float(typename E::T x);
-template <>
-__device__ __forceinline__ float to_float<Half>(__half x) {
-  return __half2float(x);
-}
-template <>
-__device__ __forceinline__ float to_float<BF16>(__nv_bfloat16 x) {
-  return __bfloat162float(x);
-}
-
-template <typename E>
-__device__ __forceinline__ float round_to(float x) {
-  return to_float<E>(from_float<E>(x));
-}
-
 // 8 x 16-bit elements = one 16-byte access.
 struct alignas(16) Vec8 {
   uint16_t h[8];

@@ -38,23 +38,6 @@ struct RopeParams {
   int num_q_heads, num_kv_heads, head_dim, slots64;
 };
 
-template <typename E>
-__device__ __forceinline__ float to_f(typename E::T x);
-template <>
-__device__ __forceinline__ float to_f<Half>(__half x) {
-  return __half2float(x);
-}
-template <>
-__device__ __forceinline__ float to_f<BF16>(__nv_bfloat16 x) {
-  return __bfloat162float(x);
-}
-
-// Round-trip through the 16-bit type (what one torch elementwise op does).
-template <typename E>
-__device__ __forceinline__ float rnd(float x) {
-  return to_f<E>(from_float<E>(x));
-}
-
 // 8 x 16-bit elements = one 16-byte access.
 struct alignas(16) Vec8 {
   uint16_t h[8];
@@ -64,7 +47,7 @@ template <typename E>
 __device__ __forceinline__ float lane_f(const Vec8& v, int i) {
   typename E::T t;
   memcpy(&t, &v.h[i], 2);
-  return to_f<E>(t);
+  return to_float<E>(t);
 }
 
 template <typename E>
@@ -135,9 +118,11 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeParams p) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float a = lane_f<E>(x1, j), b = lane_f<E>(x2, j);
-        // first half: a*cos - b*sin ; second half: b*cos + a*sin (rounded like torch)
-        lane_set<E>(lo, j, rnd<E>(a * lane_f<E>(c1, j)) + rnd<E>(-b * lane_f<E>(s1, j)));
-        lane_set<E>(hi, j, rnd<E>(b * lane_f<E>(c2, j)) + rnd<E>(a * lane_f<E>(s2, j)));
+        float l, h;
+        rope_pair<E>(a, b, lane_f<E>(c1, j), lane_f<E>(s1, j), lane_f<E>(c2, j), lane_f<E>(s2, j),
+                     l, h);
+        lane_set<E>(lo, j, l);
+        lane_set<E>(hi, j, h);
       }
       *reinterpret_cast<Vec8*>(dst + i) = lo;
       *reinterpret_cast<Vec8*>(dst + i + half) = hi;
@@ -149,11 +134,11 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeParams p) {
       }
       const T* c = reinterpret_cast<const T*>(p.cos) + t * p.cos_st;
       const T* s = reinterpret_cast<const T*>(p.sin) + t * p.sin_st;
-      const float a = to_f<E>(src[i]);
-      const float b = to_f<E>(src[i + half]);
-      dst[i] = from_float<E>(rnd<E>(a * to_f<E>(c[i])) + rnd<E>(-b * to_f<E>(s[i])));
-      dst[i + half] =
-          from_float<E>(rnd<E>(b * to_f<E>(c[i + half])) + rnd<E>(a * to_f<E>(s[i + half])));
+      float l, h;
+      rope_pair<E>(to_float<E>(src[i]), to_float<E>(src[i + half]), to_float<E>(c[i]),
+                   to_float<E>(s[i]), to_float<E>(c[i + half]), to_float<E>(s[i + half]), l, h);
+      dst[i] = from_float<E>(l);
+      dst[i + half] = from_float<E>(h);
     }
   }
 }

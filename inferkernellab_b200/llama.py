@@ -23,12 +23,12 @@ summation order.  Attention-side work is on the sm_100a kernels:
   ``:522-547``), slots and ``cu_seqlens`` come from one device
   ``build_slot_mapping`` launch per batch and the causal attention runs in
   ``paged_prefill_attention_varlen``;
-* decode runs ``paged_decode_attention``; the step's slots and lengths are
-  built once and reused by all layers;
-* in both, one ``rope_append_kv`` launch per layer applies the rotary embedding
-  to q and k (bit-identical to the reference's ``_apply_rotary``) and writes
-  the rotated K and V into the cache, in place of the reference's separate
-  rotary ops, layout copies and append;
+* decode runs ``paged_decode_attention_append``: the attention launch itself
+  applies the rotary embedding to q and to the new k and writes the new K/V
+  into the cache (bit-identical to the reference's ``_apply_rotary`` + append);
+  the step's slots and lengths are built once and reused by all layers;
+* prefill runs one ``rope_append_kv`` launch per layer (rotary on q and k, K/V
+  into the cache) before the prefill attention;
 * ``cuda_graph=True`` captures the whole decode step (every layer, lm_head)
   into one CUDA graph with device-resident metadata and replays it each step,
   instead of re-launching ~35 kernels per layer from Python every step as the
@@ -55,7 +55,7 @@ from .decode import DeviceBlockTables, _percentile
 from .ops import (
     add_rmsnorm,
     build_slot_mapping,
-    paged_decode_attention,
+    paged_decode_attention_append,
     paged_prefill_attention_varlen,
     rope_append_kv,
     silu_mul,
@@ -210,15 +210,15 @@ class LlamaPagedDecodeRunner:
             self._qkv.append(_pack_linears((attn.q_proj, attn.k_proj, attn.v_proj)))
             self._gate_up.append(_pack_linears((mlp.gate_proj, mlp.up_proj)))
 
-    def _forward(self, token_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
-                 attend) -> torch.Tensor:
+    def _forward(self, token_ids: torch.Tensor, positions: torch.Tensor, attend) -> torch.Tensor:
         """Shared layer loop on a flat token batch ``[N]``; returns the final-norm
         hidden ``[N, H]``.
 
-        Per layer: one q|k|v GEMM, one ``rope_append_kv`` (rotary on q/k, K/V
-        into ``slots``), ``attend(layer, rotated_q)``, o_proj, ``add_rmsnorm``
-        (residual add + post-attention norm), one gate|up GEMM, ``silu_mul``,
-        down_proj and ``add_rmsnorm`` into the next layer's input norm."""
+        Per layer: one q|k|v GEMM, ``attend(layer, q, k, v, cos, sin)`` (rotary,
+        K/V append and attention; q/k/v are views of the GEMM output), o_proj,
+        ``add_rmsnorm`` (residual add + post-attention norm), one gate|up GEMM,
+        ``silu_mul``, down_proj and ``add_rmsnorm`` into the next layer's input
+        norm."""
         n = token_ids.shape[0]
         inner = self.model.model
         hidden = inner.embed_tokens(token_ids.to(torch.long))
@@ -234,8 +234,7 @@ class LlamaPagedDecodeRunner:
             q = qkv[:, :qd].view(n, self.num_heads, self.head_dim)
             k = qkv[:, qd:qd + kvd].view(n, self.num_kv_heads, self.head_dim)
             v = qkv[:, qd + kvd:].view(n, self.num_kv_heads, self.head_dim)
-            q = rope_append_kv(q, k, v, cos, sin, self.cache, slots, layer=index)
-            attended = attend(index, q)
+            attended = attend(index, q, k, v, cos, sin)
             out = layer.self_attn.o_proj(attended.reshape(n, qd))
             normed, residual = add_rmsnorm(out, residual,
                                            *_norm_args(layer.post_attention_layernorm))
@@ -257,11 +256,11 @@ class LlamaPagedDecodeRunner:
         slots, _ = build_slot_mapping(tables, positions, lens, block_size=bs, num_blocks=nb,
                                       total_tokens=positions.shape[0], with_cu_seqlens=False)
 
-        def attend(layer, q):
-            return paged_decode_attention(q, self.cache, tables, lens, layer=layer,
-                                          validate_inputs=False)
+        def attend(layer, q, k, v, cos, sin):
+            return paged_decode_attention_append(q, k, v, self.cache, tables, lens, slots,
+                                                 cos=cos, sin=sin, layer=layer)
 
-        hidden = self._forward(token_ids, positions.to(torch.long), slots, attend)
+        hidden = self._forward(token_ids, positions.to(torch.long), attend)
         return self.model.lm_head(hidden)
 
     def _forward_decode(self, token_ids, requests, positions: Sequence[int]) -> torch.Tensor:
@@ -286,11 +285,12 @@ class LlamaPagedDecodeRunner:
         ids = ids.to(self.device, non_blocking=True)
         pos = pos.to(self.device, non_blocking=True)
 
-        def attend(layer, q):
+        def attend(layer, q, k, v, cos, sin):
+            q = rope_append_kv(q, k, v, cos, sin, self.cache, slots, layer=layer)
             return paged_prefill_attention_varlen(q, self.cache, tables, cu, meta[0], meta[1],
                                                   layer=layer)
 
-        return self._forward(ids, pos, slots, attend)
+        return self._forward(ids, pos, attend)
 
     # ------------------------------------------------------------------- hooks
     def _prefill(self, request: InferenceRequest, start: int, end: int) -> None:

@@ -14,6 +14,7 @@ this module                            reference (``src/inferkernellab/``)
 ``paged_prefill_attention_varlen``     (new) packed ``[sum T, Hq, D]`` form over ``cu_seqlens``
 ``build_slot_mapping``                 (new) device form of ``PagedKVCache.slot_mapping`` for a batch
 ``rope_append_kv``                     ``hf_benchmark._apply_rotary`` (:69-85) + ``append_kv_triton``
+``paged_decode_attention_append``      (new) the append (+ rotary) above fused into the decode launch
 ``add_rmsnorm`` / ``silu_mul``         (new) Transformers ``LlamaRMSNorm`` (+ residual add) and the
                                        ``act_fn(gate) * up`` of ``LlamaMLP``, one launch each
 =====================================  ==========================================================
@@ -253,6 +254,108 @@ def paged_decode_attention(query: torch.Tensor, cache, block_tables, context_len
     _lib.check(lib.b200_paged_decode(ctypes.byref(desc), ctypes.byref(args), query.data_ptr(),
                                      block_tables.data_ptr(), context_lens.data_ptr(),
                                      out.data_ptr(), ws.data_ptr(), ws.numel(), stream))
+    return out
+
+
+def _rows16(t: torch.Tensor) -> bool:
+    """Rows start on 16-byte boundaries (the fused append moves 16-byte vectors)."""
+    return (t.stride(-1) == 1 and all(st % 8 == 0 for st in t.stride()[:-1])
+            and t.data_ptr() % 16 == 0)
+
+
+def paged_decode_attention_append(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                                  cache, block_tables: torch.Tensor, context_lens: torch.Tensor,
+                                  slots: torch.Tensor, *, cos: torch.Tensor | None = None,
+                                  sin: torch.Tensor | None = None, scale=None, layer: int = 0,
+                                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode step's append and attention in one launch.
+
+    Equivalent to ``rope_append_kv(query, key, value, cos, sin, cache, slots,
+    layer)`` (or ``append_kv(key, value, cache, slots, layer)`` when ``cos`` and
+    ``sin`` are None) followed by ``paged_decode_attention(rotated_query, cache,
+    block_tables, context_lens, scale, layer, validate_inputs=False)`` -- the
+    same cache bits and the same attention output -- with the new token's K/V
+    written by the attention kernel itself just before it loads the tile that
+    holds it (reference ``hf_benchmark.py:69-85`` rotary, ``append.py:69-106``
+    append, ``triton_ops.py:404-478`` decode).  Each request's new token must be
+    its last context position (``context_lens[b] - 1``).  ``query`` ``[B, Hq, D]``
+    (un-rotated when ``cos``/``sin`` are given), ``key``/``value`` ``[B, Hkv, D]``
+    (strided views allowed), ``cos``/``sin`` ``[B, D]``, ``slots`` ``[B]``
+    int32/int64 (negative: no append for that request).
+    """
+    if query.ndim != 3 or query.device.type != "cuda":
+        raise ValueError("query must be a CUDA tensor with shape [B,H,D]")
+    batch, heads, dim = query.shape
+    layout = cache.layout
+    if key.shape != (batch, layout.num_kv_heads, dim) or value.shape != key.shape:
+        raise ValueError("key/value must have shape [B, Hkv, D] matching the cache")
+    if dim != layout.head_dim or heads % layout.num_kv_heads != 0:
+        raise ValueError("query shape does not match the cache layout")
+    if not 0 <= layer < layout.num_layers:
+        raise IndexError("layer is out of range")
+    device, dtype = query.device, cache.k.dtype
+    for t in (query, key, value):
+        if t.dtype != dtype or t.device != device:
+            raise ValueError("query/key/value must have the cache dtype and device")
+    rope = cos is not None or sin is not None
+    if rope:
+        if cos is None or sin is None:
+            raise ValueError("cos and sin must be given together")
+        cos = cos.reshape(-1, dim)
+        sin = sin.reshape(-1, dim)
+        if cos.shape[0] != batch or sin.shape[0] != batch:
+            raise ValueError("cos/sin must hold one [D] row per request")
+        if cos.dtype != dtype or sin.dtype != dtype or cos.device != device or sin.device != device:
+            raise ValueError("cos/sin must have the cache dtype and device")
+        cos, sin = (t if _rows16(t) else t.contiguous() for t in (cos, sin))
+    if slots.numel() != batch or slots.dtype not in _INDEX_CODE or slots.device != device:
+        raise ValueError("slots must be one int32/int64 entry per request on the query device")
+    block_tables = _as_index_tensor(block_tables, device)
+    context_lens = _as_index_tensor(context_lens, device)
+    if block_tables.ndim != 2 or block_tables.shape[0] != batch:
+        raise ValueError("block_tables must have shape [B, max_blocks]")
+    if context_lens.ndim != 1 or context_lens.shape[0] != batch:
+        raise ValueError("context_lens must have shape [B]")
+    if block_tables.dtype not in _INDEX_CODE or context_lens.dtype not in _INDEX_CODE:
+        raise ValueError("block_tables and context_lens must use int32 or int64")
+    if block_tables.stride(-1) != 1:
+        block_tables = block_tables.contiguous()
+    if not context_lens.is_contiguous():
+        context_lens = context_lens.contiguous()
+    slots = slots.reshape(-1)
+    if not slots.is_contiguous():
+        slots = slots.contiguous()
+    key, value = (t if _rows16(t) else t.contiguous() for t in (key, value))
+    if (query.stride(-1) != 1 or query.stride(0) % 2 or query.stride(1) % 2
+            or query.data_ptr() % 4):
+        query = query.contiguous()
+    if out is None:
+        out = torch.empty(query.shape, dtype=dtype, device=device)
+    elif (out.shape != query.shape or out.dtype != dtype or out.stride(-1) != 1
+          or out.stride(0) % 4 or out.stride(1) % 4 or out.data_ptr() % 8):
+        raise ValueError("out must match the query shape and dtype, with rows 8-byte aligned")
+    lib = _lib.load()
+    stream = _stream_ptr(device)
+    desc = _cache_desc(cache)
+    args = _lib.DecodeArgs(
+        batch, heads, block_tables.shape[1], layer, query.stride(0), query.stride(1),
+        out.stride(0), out.stride(1), block_tables.stride(0), _INDEX_CODE[block_tables.dtype],
+        _INDEX_CODE[context_lens.dtype],
+        float(scale) if scale is not None else layout.head_dim ** -0.5)
+    fused = _lib.DecodeAppendArgs(
+        1 if rope else 0, _INDEX_CODE[slots.dtype], key.stride(0), key.stride(1),
+        value.stride(0), value.stride(1), cos.stride(0) if rope else 0,
+        sin.stride(0) if rope else 0)
+    need = lib.b200_paged_decode_workspace_bytes(ctypes.byref(desc), ctypes.byref(args))
+    if need == 0:
+        _lib.check(_lib.B200_ERR_INVALID if _lib.last_error() else _lib.B200_ERR_CUDA)
+    ws = _WORKSPACES.get(device, stream.value or 0, need,
+                         (heads // layout.num_kv_heads, layout.head_dim, dtype))
+    _lib.check(lib.b200_paged_decode_append(
+        ctypes.byref(desc), ctypes.byref(args), ctypes.byref(fused), query.data_ptr(),
+        key.data_ptr(), value.data_ptr(), cos.data_ptr() if rope else None,
+        sin.data_ptr() if rope else None, slots.data_ptr(), block_tables.data_ptr(),
+        context_lens.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(), stream))
     return out
 
 
