@@ -12,7 +12,8 @@ operators plus host mirrors of its cache, scheduler and runtime:
   causal prefill over the paged cache;
 * ``build_slot_mapping`` -- device-built slots + ``cu_seqlens`` for a batch;
 * ``PagedKVCache``, ``BlockAllocator``, ``TokenBudgetScheduler``,
-  ``InferenceRuntime`` -- the reference's host-side contract.
+  ``InferenceRuntime`` -- the reference's host-side contract;
+* ``PrefixCache`` -- prefix sharing: refcounted blocks indexed by prompt content.
 
 Backend names for the reference runners: ``BACKEND_NAME`` (attention) and
 ``APPEND_BACKEND_NAME`` (append).  The kernels live in
@@ -34,6 +35,7 @@ from .ops import (
     rope_append_kv,
     silu_mul,
 )
+from .prefix_cache import PrefixCache
 from .runtime import InferenceRuntime, RuntimeStats
 from .scheduler import InferenceRequest, ScheduleBatch, TokenBudgetScheduler
 
@@ -53,6 +55,7 @@ __all__ = [
     "InferenceRequest",
     "InferenceRuntime",
     "PagedKVCache",
+    "PrefixCache",
     "RuntimeStats",
     "ScheduleBatch",
     "TokenBudgetScheduler",

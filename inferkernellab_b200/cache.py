@@ -31,11 +31,17 @@ class CacheLayout:
 
 
 class BlockAllocator:
-    """Deterministic physical-block allocator with owner tracking.
+    """Deterministic physical-block allocator with owner tracking and sharing.
 
     ``allocate`` hands out the lowest never-used ids first (0, 1, 2, ...) and
     reuses freed ids last-freed-first, matching reference ``cache.py:17-64``;
     ``free`` validates the whole request before releasing anything.
+
+    Blocks carry a reference count (prefix sharing, ``prefix_cache.py``):
+    ``share`` adds a holder to allocated blocks and ``free`` drops one; a block
+    returns to the free stack when its last holder frees it.  A block with a
+    single holder behaves exactly as in the reference (same order, same owner
+    checks); the owner check is skipped for blocks that are shared.
     """
 
     def __init__(self, num_blocks: int):
@@ -46,6 +52,7 @@ class BlockAllocator:
         self._stack = list(range(num_blocks - 1, -1, -1))
         self._in_use: set[int] = set()
         self._owner_of: dict[int, int] = {}
+        self._refs: dict[int, int] = {}
 
     @property
     def num_free_blocks(self) -> int:
@@ -62,6 +69,7 @@ class BlockAllocator:
             raise RuntimeError(f"out of KV blocks: requested={count}, free={len(self._stack)}")
         taken = [self._stack.pop() for _ in range(count)]
         self._in_use.update(taken)
+        self._refs.update((block, 1) for block in taken)
         if owner is not None:
             self._owner_of.update((block, owner) for block in taken)
         return taken
@@ -75,12 +83,31 @@ class BlockAllocator:
                 raise ValueError(f"invalid block id: {block}")
             if block not in self._in_use:
                 raise ValueError(f"block {block} is not allocated")
-            if owner is not None and self._owner_of.get(block) != owner:
+            if (owner is not None and self._refs.get(block, 1) == 1
+                    and self._owner_of.get(block) != owner):
                 raise ValueError(f"block {block} is not owned by request {owner}")
         for block in ids:
+            refs = self._refs.get(block, 1) - 1
+            if refs > 0:
+                self._refs[block] = refs
+                continue
+            self._refs.pop(block, None)
             self._in_use.discard(block)
             self._owner_of.pop(block, None)
             self._stack.append(block)
+
+    def share(self, block_ids) -> None:
+        """Add one holder to each allocated block of ``block_ids``."""
+        ids = tuple(block_ids)
+        for block in ids:
+            if not isinstance(block, int) or block not in self._in_use:
+                raise ValueError(f"block {block} is not allocated")
+        for block in ids:
+            self._refs[block] = self._refs.get(block, 1) + 1
+
+    def ref_count(self, block_id: int) -> int:
+        """Holders of ``block_id`` (0 when it is free)."""
+        return self._refs.get(block_id, 0) if block_id in self._in_use else 0
 
     def owner(self, block_id: int) -> int | None:
         return self._owner_of.get(block_id)

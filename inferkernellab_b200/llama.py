@@ -52,6 +52,7 @@ import torch
 
 from .cache import PagedKVCache
 from .decode import DeviceBlockTables, _percentile
+from .prefix_cache import PrefixCache
 from .ops import (
     add_rmsnorm,
     build_slot_mapping,
@@ -89,6 +90,7 @@ class LlamaPagedRunResult:
     token_logprobs: tuple[tuple[float, ...], ...] = ()
     sampling_logprobs: tuple[tuple[float, ...], ...] = ()
     finish_reasons: tuple[str, ...] = ()
+    prefix_cached_tokens: int = 0  # prompt tokens served from shared blocks (prefix_caching)
 
     @property
     def decode_p50_ms(self) -> float:
@@ -119,7 +121,7 @@ class LlamaPagedDecodeRunner:
                  temperature: float = 0.0, top_p: float = 1.0, seed: int = 2026,
                  eos_token_ids: Sequence[int] | None = None,
                  token_exchange: TokenExchange | None = None, collect_logits: bool = True,
-                 cuda_graph: bool = False):
+                 cuda_graph: bool = False, prefix_caching: bool = False):
         if not prompts:
             raise ValueError("at least one prompt is required")
         if max_new_tokens <= 0:
@@ -169,12 +171,14 @@ class LlamaPagedDecodeRunner:
                                   num_layers=self.num_layers, dtype=self.dtype, device=self.device)
         scheduler = TokenBudgetScheduler(max_num_seqs=len(self.prompts),
                                          max_num_batched_tokens=max_num_batched_tokens)
+        self.prefix_cache = PrefixCache(self.cache.allocator, block_size) if prefix_caching else None
         self.runtime = InferenceRuntime(
             self.cache, scheduler,
             prefill_fn=self._prefill if prefill_mode == "token" else None,
             prefill_batch_fn=self._prefill_batch if prefill_mode == "batched" else None,
-            decode_fn=self._decode)
-        self.requests = [self.runtime.submit(rid, len(p), max_new_tokens)
+            decode_fn=self._decode, prefix_cache=self.prefix_cache)
+        self.requests = [self.runtime.submit(rid, len(p), max_new_tokens,
+                                             token_ids=p if prefix_caching else None)
                          for rid, p in enumerate(self.prompts)]
         width = max(1, max(-(-(n + max_new_tokens) // block_size) for n in self.prompt_lengths))
         self.meta = DeviceBlockTables(len(self.requests), width, self.device)
@@ -410,6 +414,8 @@ class LlamaPagedDecodeRunner:
                     decode_ms.append(elapsed)
                 else:
                     raise RuntimeError("scheduler became idle before all requests finished")
+        if self.prefix_cache is not None:
+            self.prefix_cache.clear()  # the index holds one reference per cached block
         cache_released = self.cache.allocator.num_used_blocks == 0
         if len(self._prompt_logits) != len(self.requests):
             raise RuntimeError("prefill did not produce one final logits tensor per request")
@@ -438,7 +444,8 @@ class LlamaPagedDecodeRunner:
             tpot_wall_ms=sum(decode_ms) / len(decode_ms),
             peak_memory_allocated_bytes=int(torch.cuda.max_memory_allocated(self.device)),
             peak_kv_memory_bytes=peak_kv, used_blocks_peak=used_peak,
-            cache_released=cache_released and self.cache.allocator.num_used_blocks == 0)
+            cache_released=cache_released and self.cache.allocator.num_used_blocks == 0,
+            prefix_cached_tokens=self.runtime.prefix_cached_tokens)
 
 
 class _DecodeGraph:

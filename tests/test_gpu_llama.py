@@ -102,3 +102,21 @@ def test_llama_cuda_graph_decode_matches_eager_decode():
         assert torch.allclose(a, b, atol=1e-3, rtol=0)
     assert graph.cache_released
     _assert_ok(correctness(model, prompts, graph))
+
+
+def test_llama_prefix_caching_gives_the_unshared_results():
+    """Prompts with a common 40-token prefix: with prefix caching the later budget
+    batches reuse the first request's blocks and prefill only their own tokens;
+    tokens and logits match the unshared run (and the eager oracle)."""
+    model = _model(torch.bfloat16, num_kv_heads=2, num_layers=2, hidden=128, heads=4)
+    common = [(3 * j + 1) % 128 for j in range(40)]
+    prompts = (tuple(common + [5, 6, 7]), tuple(common + [9] * 12), tuple(common),
+               tuple(common[:20] + [1, 2, 3]))
+    kwargs = dict(max_new_tokens=4, block_size=8, max_num_batched_tokens=48)
+    plain = LlamaPagedDecodeRunner(model, prompts, **kwargs).run()
+    shared = LlamaPagedDecodeRunner(model, prompts, prefix_caching=True, **kwargs).run()
+    assert shared.prefix_cached_tokens > 0
+    assert shared.generated_tokens == plain.generated_tokens
+    assert torch.allclose(shared.prompt_logits, plain.prompt_logits, atol=3e-2, rtol=0)
+    _assert_ok(correctness(model, prompts, shared))
+    assert shared.cache_released
