@@ -165,8 +165,9 @@ B200_API int b200_append_kv(const b200_cache_desc* cache, int32_t layer, const v
  * context position, context_lens[b] - 1 (a decode step).  query is the
  * un-rotated query when rope = 1; key/value [B, Hkv, D] (strides below); cos/sin
  * [B, D] rows of the rotary table for each request's new position (rope = 1);
- * key/value/cos/sin rows 16-byte aligned; slots [B] (negative = skip the
- * append).  The cache holds
+ * key/value/cos/sin rows 16-byte aligned, and with rope also query and out rows
+ * (the rotated query is staged in out before the output overwrites it); slots
+ * [B] (negative = skip the append).  The cache holds
  * exactly what the separate calls would write; the output matches
  * b200_paged_decode on the rotated query.  Workspace as b200_paged_decode.
  */

@@ -258,6 +258,11 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Arrive on a named barrier without waiting (the other side uses bar.sync).
+__device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Load an index from an int32 or int64 array.
 __device__ __forceinline__ long long load_index(const void* base, long long i, bool is64) {
   return is64 ? reinterpret_cast<const long long*>(base)[i]

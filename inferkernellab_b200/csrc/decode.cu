@@ -64,8 +64,8 @@ struct DecodeParams {
   // Fused new-token append (b200_paged_decode_append); fuse_append == 0 = off.
   // The new token of request r is its last context position (lens[r] - 1): the
   // CTA that owns the tile holding that position writes its K (rotated when
-  // rope) and V at new_slots[r] before its first TMA load; with rope the
-  // consumers rotate q.
+  // rope) and V at new_slots[r] before its first TMA load; with rope every CTA
+  // also stages the rotated q of its segments in `out`.
   int fuse_append, rope, slots64;
   const void* new_k;
   const void* new_v;
@@ -167,150 +167,157 @@ struct TileCursor {
   }
 };
 
-// All threads of the CTA, before any TMA load: write the new token (position
-// len - 1) of every segment whose last tile lies in [my_begin, my_end).  Only
-// this CTA loads that tile, so no other CTA can read the token's cache row.  K
-// is rotated with the reference's rounding when p.rope, V is copied; 16-byte
-// vectors (the host checks the alignment).  Each thread loads all it needs for
-// an item before it stores, so one item costs one memory round trip.
-template <typename E, int D>
-__device__ __forceinline__ void append_range_tokens(const DecodeParams& p, const int* begin_s,
-                                                    const int* len_s, int my_begin, int my_end) {
+// The consumer warps, while the producer already streams the first tiles:
+//  * write the new token (position len - 1) of every segment whose last tile
+//    lies in [my_begin, my_end) -- only this CTA loads that tile, so no other CTA
+//    can read the token's cache row.  K is rotated with the reference's rounding
+//    when p.rope, V is copied;
+//  * with p.rope, rotate the query heads of every segment the range touches and
+//    stage them in the segment's own rows of `out` (the consumers read q from
+//    there).  A segment's output is written only after every CTA working on it
+//    has passed this prologue, and CTAs sharing a split segment write identical
+//    bits here.
+// 16-byte vectors (the host checks the alignment); every item issues its data
+// loads before the slot load, so it costs one memory round trip.
+template <typename E>
+__device__ __forceinline__ void rope_vec8(const uint4& a4, const uint4& b4, const uint4& cl4,
+                                          const uint4& ch4, const uint4& sl4, const uint4& sh4,
+                                          uint4& lo4, uint4& hi4) {
   using T = typename E::T;
-  constexpr int kVec = D / 8;         // 16-byte vectors per cache row
-  constexpr int kItems = 2 * kVec;    // V vectors, then K vectors (rope: K vector pairs)
+  const T* a = reinterpret_cast<const T*>(&a4);
+  const T* b = reinterpret_cast<const T*>(&b4);
+  const T* cl = reinterpret_cast<const T*>(&cl4);
+  const T* ch = reinterpret_cast<const T*>(&ch4);
+  const T* sl = reinterpret_cast<const T*>(&sl4);
+  const T* sh = reinterpret_cast<const T*>(&sh4);
+  T* lo = reinterpret_cast<T*>(&lo4);
+  T* hi = reinterpret_cast<T*>(&hi4);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    float l, u;
+    rope_pair<E>(to_float<E>(a[e]), to_float<E>(b[e]), to_float<E>(cl[e]), to_float<E>(sl[e]),
+                 to_float<E>(ch[e]), to_float<E>(sh[e]), l, u);
+    lo[e] = from_float<E>(l);
+    hi[e] = from_float<E>(u);
+  }
+}
+
+template <typename E, int D>
+__device__ __forceinline__ void fused_prologue(const DecodeParams& p, const int* begin_s,
+                                               const int* len_s, int my_begin, int my_end,
+                                               int thread, int nthreads) {
+  using T = typename E::T;
+  constexpr int kVec = D / 8;    // 16-byte vectors per row
+  constexpr int kHalf = kVec / 2;
+  constexpr int kUnroll = 4;     // items per thread whose loads are in flight together
   const int hkv = p.num_kv_heads;
+  const int kv_items = 2 * kVec;                       // V vectors, then K vectors / pairs
+  const int q_items = p.rope ? p.group * kHalf : 0;    // rotary pairs of the G query heads
+  const int per_seg = kv_items + q_items;
   TileCursor first, last;
   first.init(my_begin, begin_s, len_s, p.num_seqs, hkv);
   last.init(my_end - 1, begin_s, len_s, p.num_seqs, hkv);
   const int g0 = first.r * hkv + first.h;
-  const int nseg = last.r * hkv + last.h - g0 + 1;
-  for (int it = threadIdx.x; it < nseg * kItems; it += blockDim.x) {
-    const int k = it / kItems;
-    const int item = it - k * kItems;
-    const int g = g0 + k;
-    const int r = g / hkv;
-    const int h = g - r * hkv;
-    const int len = len_s[r];
-    if (len == 0) continue;
-    const int nt = (len + kDecTile - 1) / kDecTile;
-    const int last_tile = begin_s[r] + h * nt + nt - 1;
-    if (last_tile < my_begin || last_tile >= my_end) continue;
-    const long long slot = load_index(p.new_slots, r, p.slots64);
-    if (slot < 0) continue;  // padding slot: nothing to append
-    if (slot >= p.slots_per_layer) {
-      if (item == 0 && p.err) atomicOr(p.err, kErrBadSlot);
-      continue;
+  const int total = (last.r * hkv + last.h - g0 + 1) * per_seg;
+  enum : int { kNone = 0, kV = 1, kK = 2, kQ = 3 };
+  for (int base = thread; base < total; base += nthreads * kUnroll) {
+    int kind[kUnroll], r_[kUnroll], h_[kUnroll], j_[kUnroll];
+    long long slot[kUnroll], head_[kUnroll];
+    uint4 x0[kUnroll], x1[kUnroll], c0[kUnroll], c1[kUnroll], s0[kUnroll], s1[kUnroll];
+    // Phase 1: decode every item and issue all of its loads.
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      kind[u] = kNone;
+      const int it = base + u * nthreads;
+      if (it >= total) continue;
+      const int k = it / per_seg;
+      const int item = it - k * per_seg;
+      const int g = g0 + k;
+      const int r = g / hkv;
+      const int h = g - r * hkv;
+      const int len = len_s[r];
+      if (len == 0) continue;
+      r_[u] = r;
+      h_[u] = h;
+      const bool rope = p.rope != 0;
+      if (item >= kv_items) {
+        const int qi = item - kv_items;
+        const int qh = qi / kHalf;
+        const int j = qi - qh * kHalf;
+        const long long head = static_cast<long long>(h) * p.group + qh;
+        const uint4* qs = reinterpret_cast<const uint4*>(
+            reinterpret_cast<const T*>(p.q) + r * p.q_stride_seq + head * p.q_stride_head);
+        x0[u] = qs[j];
+        x1[u] = qs[j + kHalf];
+        j_[u] = j;
+        head_[u] = head;
+        kind[u] = kQ;
+      } else {
+        const int nt = (len + kDecTile - 1) / kDecTile;
+        const int last_tile = begin_s[r] + h * nt + nt - 1;
+        if (last_tile < my_begin || last_tile >= my_end) continue;
+        if (item < kVec) {
+          x0[u] = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.new_v) +
+                                                 r * p.nv_stride_seq + h * p.nv_stride_head)[item];
+          j_[u] = item;
+          kind[u] = kV;
+        } else {
+          const int j = item - kVec;
+          if (rope && j >= kHalf) continue;  // the pair (j, j + D/16) is handled by item j
+          const uint4* ks = reinterpret_cast<const uint4*>(
+              reinterpret_cast<const T*>(p.new_k) + r * p.nk_stride_seq + h * p.nk_stride_head);
+          x0[u] = ks[j];
+          if (rope) x1[u] = ks[j + kHalf];
+          j_[u] = j;
+          kind[u] = kK;
+        }
+        slot[u] = load_index(p.new_slots, r, p.slots64);
+      }
+      if (rope && kind[u] != kV) {
+        const uint4* cv = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.cos) +
+                                                         r * p.cos_stride);
+        const uint4* sv = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.sin) +
+                                                         r * p.sin_stride);
+        const int j = j_[u];
+        c0[u] = cv[j];
+        c1[u] = cv[j + kHalf];
+        s0[u] = sv[j];
+        s1[u] = sv[j + kHalf];
+      }
     }
-    const long long row = ((p.layer_slot_base + slot) * hkv + h) * D;
-    if (item < kVec) {
-      const uint4* vs = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.new_v) +
-                                                       r * p.nv_stride_seq + h * p.nv_stride_head);
-      reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.v_cache) + row)[item] = vs[item];
-      continue;
-    }
-    const int j = item - kVec;
-    const uint4* ks = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.new_k) +
-                                                     r * p.nk_stride_seq + h * p.nk_stride_head);
-    uint4* kd = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.k_cache) + row);
-    if (!p.rope) {
-      kd[j] = ks[j];
-      continue;
-    }
-    if (j >= kVec / 2) continue;  // the pair (j, j + D/16) is handled by item j
-    const uint4* cv = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.cos) +
-                                                     r * p.cos_stride);
-    const uint4* sv = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.sin) +
-                                                     r * p.sin_stride);
-    const uint4 a4 = ks[j], b4 = ks[j + kVec / 2];
-    const uint4 cl4 = cv[j], ch4 = cv[j + kVec / 2], sl4 = sv[j], sh4 = sv[j + kVec / 2];
-    const T* a = reinterpret_cast<const T*>(&a4);
-    const T* b = reinterpret_cast<const T*>(&b4);
-    const T* cl = reinterpret_cast<const T*>(&cl4);
-    const T* ch = reinterpret_cast<const T*>(&ch4);
-    const T* sl = reinterpret_cast<const T*>(&sl4);
-    const T* sh = reinterpret_cast<const T*>(&sh4);
-    uint4 lo4, hi4;
-    T* lo = reinterpret_cast<T*>(&lo4);
-    T* hi = reinterpret_cast<T*>(&hi4);
+    // Phase 2: rotate and store.
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float l, u;
-      rope_pair<E>(to_float<E>(a[e]), to_float<E>(b[e]), to_float<E>(cl[e]), to_float<E>(sl[e]),
-                   to_float<E>(ch[e]), to_float<E>(sh[e]), l, u);
-      lo[e] = from_float<E>(l);
-      hi[e] = from_float<E>(u);
-    }
-    kd[j] = lo4;
-    kd[j + kVec / 2] = hi4;
-  }
-}
-
-// Rotate one pair of fragment registers: `lo` holds q[d], q[d+1] and `hi` holds
-// q[d+D/2], q[d+D/2+1] of the same head (the two halves of a rotary pair always
-// land in the same thread of an m16n8k16 fragment).
-template <typename E>
-__device__ __forceinline__ void rope_frag_pair(uint32_t& lo, uint32_t& hi, const typename E::T* c,
-                                               const typename E::T* sn, int d, int half) {
-  using T = typename E::T;
-  const uint32_t cl = *reinterpret_cast<const uint32_t*>(c + d);
-  const uint32_t ch = *reinterpret_cast<const uint32_t*>(c + d + half);
-  const uint32_t sl = *reinterpret_cast<const uint32_t*>(sn + d);
-  const uint32_t sh = *reinterpret_cast<const uint32_t*>(sn + d + half);
-  auto elem = [](uint32_t v, int e) {
-    const uint16_t bits = static_cast<uint16_t>(e ? v >> 16 : v & 0xffffu);
-    T t;
-    memcpy(&t, &bits, 2);
-    return to_float<E>(t);
-  };
-  float l0, h0, l1, h1;
-  rope_pair<E>(elem(lo, 0), elem(hi, 0), elem(cl, 0), elem(sl, 0), elem(ch, 0), elem(sh, 0), l0,
-               h0);
-  rope_pair<E>(elem(lo, 1), elem(hi, 1), elem(cl, 1), elem(sl, 1), elem(ch, 1), elem(sh, 1), l1,
-               h1);
-  lo = pack2<E>(l0, l1);
-  hi = pack2<E>(h0, h1);
-}
-
-// Rotary embedding of the query fragments of one segment.  Register (kk, j)
-// holds dims d = 16*kk + 8*j + 2*tq (+1); its partner d + D/2 is register
-// (kk + D/32, j) for D >= 32 and (kk, 1) for D = 16.
-template <typename E, int D, int NT>
-__device__ __forceinline__ void rope_qT_frag(uint32_t (&qb)[NT][D / 16][2],
-                                             const typename E::T* c, const typename E::T* sn,
-                                             int lane) {
-  const int tq = lane & 3;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    if constexpr (D >= 32) {
-#pragma unroll
-      for (int kk = 0; kk < D / 32; ++kk)
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-          rope_frag_pair<E>(qb[nt][kk][j], qb[nt][kk + D / 32][j], c, sn, 16 * kk + 8 * j + 2 * tq,
-                            D / 2);
-    } else {
-      rope_frag_pair<E>(qb[nt][0][0], qb[nt][0][1], c, sn, 2 * tq, D / 2);
-    }
-  }
-}
-
-// Same for the heads-as-M A fragments: qf[kk][0|2] = row g, qf[kk][1|3] = row g + 8.
-template <typename E, int D>
-__device__ __forceinline__ void rope_q_frag(uint32_t (&qf)[D / 16][4], const typename E::T* c,
-                                            const typename E::T* sn, int lane) {
-  const int tq = lane & 3;
-#pragma unroll
-  for (int row = 0; row < 2; ++row) {
-    if constexpr (D >= 32) {
-#pragma unroll
-      for (int kk = 0; kk < D / 32; ++kk)
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-          rope_frag_pair<E>(qf[kk][2 * j + row], qf[kk + D / 32][2 * j + row], c, sn,
-                            16 * kk + 8 * j + 2 * tq, D / 2);
-    } else {
-      rope_frag_pair<E>(qf[0][row], qf[0][2 + row], c, sn, 2 * tq, D / 2);
+    for (int u = 0; u < kUnroll; ++u) {
+      if (kind[u] == kNone) continue;
+      const int r = r_[u], h = h_[u], j = j_[u];
+      if (kind[u] == kQ) {
+        uint4 lo, hi;
+        rope_vec8<E>(x0[u], x1[u], c0[u], c1[u], s0[u], s1[u], lo, hi);
+        uint4* qd = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + r * p.out_stride_seq +
+                                             head_[u] * p.out_stride_head);
+        qd[j] = lo;
+        qd[j + kHalf] = hi;
+        continue;
+      }
+      if (slot[u] < 0) continue;  // padding slot: nothing to append
+      if (slot[u] >= p.slots_per_layer) {
+        if (kind[u] == kV && j == 0 && p.err) atomicOr(p.err, kErrBadSlot);
+        continue;
+      }
+      const long long row = ((p.layer_slot_base + slot[u]) * hkv + h) * D;
+      if (kind[u] == kV) {
+        reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.v_cache) + row)[j] = x0[u];
+        continue;
+      }
+      uint4* kd = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.k_cache) + row);
+      if (p.rope) {
+        uint4 lo, hi;
+        rope_vec8<E>(x0[u], x1[u], c0[u], c1[u], s0[u], s1[u], lo, hi);
+        kd[j] = lo;
+        kd[j + kHalf] = hi;
+      } else {
+        kd[j] = x0[u];
+      }
     }
   }
 }
@@ -453,11 +460,18 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   const int my_end = min(total, my_begin + per_cta);
   const int n_tiles = my_end - my_begin;
   if (n_tiles <= 0) return;
+  // Fused append: the consumers write the new tokens (and stage the rotated q)
+  // while the producer streams; the producer waits on named barrier 2 only
+  // before the first tile that holds a new token.
+  constexpr uint32_t kBarAppended = 2;
   if constexpr (FUSED) {
-    append_range_tokens<E, D>(p, begin_s, len_s, my_begin, my_end);
-    // Generic-proxy cache writes -> visible to this CTA's TMA loads.
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-    __syncthreads();
+    if (warp < kDecConsumerWarps) {
+      fused_prologue<E, D>(p, begin_s, len_s, my_begin, my_end, tid, kDecConsumerWarps * 32);
+      // Generic-proxy cache writes -> visible to the producer's TMA loads.
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      named_bar_arrive(kBarAppended, kDecThreads);
+      named_bar_sync(1, kDecConsumerWarps * 32);  // staged q visible to every consumer
+    }
   }
 
   const uint32_t smem_base = smem_u32(smem);
@@ -480,7 +494,12 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
     TileCursor cur;
     cur.init(my_begin, begin_s, len_s, B, HKV);
     int issued = 0;
+    bool appended = !FUSED;
     for (int it = 0; it < n_tiles; ++it) {
+      if (FUSED && !appended && cur.t == cur.nt - 1) {
+        named_bar_sync(kBarAppended, kDecThreads);  // the consumers wrote the new tokens
+        appended = true;
+      }
       const int s = it % kStages;
       const uint32_t k = static_cast<uint32_t>(it / kStages);
       if (!mbar_wait_bounded(&empty_bar[s], (k & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty))
@@ -495,6 +514,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       ++issued;
       cur.advance(len_s, B, HKV);
     }
+    if (FUSED && !appended) named_bar_sync(kBarAppended, kDecThreads);
     // Drain: the last phases this warp armed must complete before the CTA
     // exits (bounded; only waits after an abort left stages unconsumed).
     if (lane == 0) drain_stages<kStages>(full_bar, issued, p.err);
@@ -527,13 +547,15 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   for (int it = 0; it < n_tiles; ++it) {
     if (seg_start) {
       seg_start = false;
-      const T* qg = reinterpret_cast<const T*>(p.q) + cur.r * p.q_stride_seq +
-                    static_cast<long long>(cur.h * G) * p.q_stride_head;
+      // With the fused rotary append, the prologue staged the rotated q in `out`.
+      const bool staged = FUSED && p.rope;
+      const T* qg = staged ? reinterpret_cast<const T*>(p.out) + cur.r * p.out_stride_seq +
+                                 static_cast<long long>(cur.h * G) * p.out_stride_head
+                           : reinterpret_cast<const T*>(p.q) + cur.r * p.q_stride_seq +
+                                 static_cast<long long>(cur.h * G) * p.q_stride_head;
+      const long long q_head_stride = staged ? p.out_stride_head : p.q_stride_head;
       if constexpr (kTrans) {
-        load_qT_frag<E, D, NT>(qb, qg, p.q_stride_head, G, lane);
-        if (FUSED && p.rope)
-          rope_qT_frag<E, D, NT>(qb, reinterpret_cast<const T*>(p.cos) + cur.r * p.cos_stride,
-                                 reinterpret_cast<const T*>(p.sin) + cur.r * p.sin_stride, lane);
+        load_qT_frag<E, D, NT>(qb, qg, q_head_stride, G, lane);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -542,11 +564,8 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
           l_t[nt][0] = l_t[nt][1] = 0.f;
         }
       } else {
-        load_q_frag<E, D>(qf, row0 < G ? qg + row0 * p.q_stride_head : nullptr,
-                          row1 < G ? qg + row1 * p.q_stride_head : nullptr, tq);
-        if (FUSED && p.rope)
-          rope_q_frag<E, D>(qf, reinterpret_cast<const T*>(p.cos) + cur.r * p.cos_stride,
-                            reinterpret_cast<const T*>(p.sin) + cur.r * p.sin_stride, lane);
+        load_q_frag<E, D>(qf, row0 < G ? qg + row0 * q_head_stride : nullptr,
+                          row1 < G ? qg + row1 * q_head_stride : nullptr, tq);
 #pragma unroll
         for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
         m_r[0] = m_r[1] = -INFINITY;
@@ -993,6 +1012,11 @@ static int launch_decode_common(const b200_cache_desc* c, const b200_decode_args
       if (((reinterpret_cast<uintptr_t>(f->cos) | reinterpret_cast<uintptr_t>(f->sin)) & 15) ||
           ((fa->cos_stride_seq | fa->sin_stride_seq) & 7))
         return set_error(B200_ERR_INVALID, "cos/sin rows must be 16-byte aligned");
+      // The rotated query is staged in `out` with 16-byte vectors.
+      if (((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(out)) & 15) ||
+          ((a->q_stride_seq | a->q_stride_head | a->out_stride_seq | a->out_stride_head) & 7))
+        return set_error(B200_ERR_INVALID,
+                         "with rope, query and out rows must be 16-byte aligned");
     }
   }
   if (!query || !block_tables || !context_lens || !out || !c->k_cache || !c->v_cache)

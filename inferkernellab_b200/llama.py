@@ -56,6 +56,7 @@ from .prefix_cache import PrefixCache
 from .ops import (
     add_rmsnorm,
     build_slot_mapping,
+    paged_decode_attention,
     paged_decode_attention_append,
     paged_prefill_attention_varlen,
     rope_append_kv,
@@ -121,7 +122,8 @@ class LlamaPagedDecodeRunner:
                  temperature: float = 0.0, top_p: float = 1.0, seed: int = 2026,
                  eos_token_ids: Sequence[int] | None = None,
                  token_exchange: TokenExchange | None = None, collect_logits: bool = True,
-                 cuda_graph: bool = False, prefix_caching: bool = False):
+                 cuda_graph: bool = False, prefix_caching: bool = False,
+                 sync_steps: bool = True, fused_decode: bool | str = "auto"):
         if not prompts:
             raise ValueError("at least one prompt is required")
         if max_new_tokens <= 0:
@@ -157,6 +159,24 @@ class LlamaPagedDecodeRunner:
         self.token_exchange = token_exchange
         self.collect_logits = collect_logits
         self.cuda_graph = cuda_graph
+        # sync_steps=True times every step to its device completion (the
+        # reference's per-step wall clock); False lets the host prepare the next
+        # step while the device still runs this one (throughput measurement; the
+        # per-step figures then split the same total differently).
+        self.sync_steps = sync_steps
+        # fused_decode: rotary + append inside the attention launch
+        # (paged_decode_attention_append); False: rope_append_kv, then
+        # paged_decode_attention (two launches per layer, same results).  "auto"
+        # fuses when the step has at most two (request, kv head) segments per
+        # resident decode CTA: the fused kernel stages every segment's rotated
+        # q before it streams, which pays off for few long segments (one B200:
+        # 193.3 vs 196.2 us at 64 requests of ctx U[1,8192]) but not for many
+        # short ones (122.8 vs 119.1 us at 256 requests of ctx ~540).
+        if fused_decode not in (True, False, "auto"):
+            raise ValueError("fused_decode must be True, False or 'auto'")
+        self.fused_decode = fused_decode
+        self._host_tokens = torch.empty(len(prompts), dtype=torch.long, pin_memory=True)
+        self._tokens_ready = torch.cuda.Event()
         self._graph: _DecodeGraph | None = None
         self.prompt_lengths = tuple(len(p) for p in self.prompts)
         cfg = model.config
@@ -260,7 +280,15 @@ class LlamaPagedDecodeRunner:
         slots, _ = build_slot_mapping(tables, positions, lens, block_size=bs, num_blocks=nb,
                                       total_tokens=positions.shape[0], with_cu_seqlens=False)
 
+        fused = self.fused_decode
+        if fused == "auto":
+            fused = positions.shape[0] * self.num_kv_heads <= 2 * _decode_ctas(self.device)
+
         def attend(layer, q, k, v, cos, sin):
+            if not fused:
+                q = rope_append_kv(q, k, v, cos, sin, self.cache, slots, layer=layer)
+                return paged_decode_attention(q, self.cache, tables, lens, layer=layer,
+                                              validate_inputs=False)
             return paged_decode_attention_append(q, k, v, self.cache, tables, lens, slots,
                                                  cos=cos, sin=sin, layer=layer)
 
@@ -368,6 +396,11 @@ class LlamaPagedDecodeRunner:
             next_tokens = torch.stack([s[0] for s in sampled]).to(torch.long)
         if self.token_exchange is not None:
             self.token_exchange(next_tokens)
+        # Copy the sampled ids out before the step's model work is queued, so the
+        # host waits for the sampling only, not for the whole forward pass.
+        host_tokens = self._host_tokens[:len(requests)]
+        host_tokens.copy_(next_tokens, non_blocking=True)
+        self._tokens_ready.record()
         positions = [r.prompt_tokens + r.generated_tokens for r in requests]
         ids = [r.request_id for r in requests]
         if self.cuda_graph and ids == list(range(len(ids))):
@@ -377,7 +410,8 @@ class LlamaPagedDecodeRunner:
             next_logits = self._graph.replay(next_tokens, positions)
         else:
             next_logits = self._forward_decode(next_tokens, requests, positions)
-        tokens = next_tokens.tolist()
+        self._tokens_ready.synchronize()
+        tokens = host_tokens.tolist()
         for row, request in enumerate(requests):
             token = int(tokens[row])
             self._generated[request.request_id].append(token)
@@ -393,7 +427,8 @@ class LlamaPagedDecodeRunner:
     def _timed_step(self):
         started = time.perf_counter()
         batch = self.runtime.step()
-        torch.cuda.synchronize(self.device)
+        if self.sync_steps or batch.phase != "decode":
+            torch.cuda.synchronize(self.device)
         return batch, (time.perf_counter() - started) * 1000
 
     def run(self) -> LlamaPagedRunResult:
@@ -414,6 +449,10 @@ class LlamaPagedDecodeRunner:
                     decode_ms.append(elapsed)
                 else:
                     raise RuntimeError("scheduler became idle before all requests finished")
+            if decode_ms and not self.sync_steps:  # the last step's device work
+                started = time.perf_counter()
+                torch.cuda.synchronize(self.device)
+                decode_ms[-1] += (time.perf_counter() - started) * 1000
         if self.prefix_cache is not None:
             self.prefix_cache.clear()  # the index holds one reference per cached block
         cache_released = self.cache.allocator.num_used_blocks == 0
@@ -467,7 +506,13 @@ class _DecodeGraph:
         self.tables = runner.meta.rows(requests)
         self.tokens = tokens.detach().clone().to(torch.long)
         self.positions = torch.tensor(list(positions), dtype=torch.int32, device=device)
-        self._host_pos = torch.empty(self.batch, dtype=torch.int32, pin_memory=True)
+        # Two pinned staging buffers, used in turn: with the runner's sync_steps=False
+        # the host writes step N+1's positions while step N's copy may still be
+        # queued; it last used this buffer two steps ago, whose copy has run (the
+        # host has since waited for a later step's sampled tokens).
+        self._host_pos = [torch.empty(self.batch, dtype=torch.int32, pin_memory=True)
+                          for _ in range(2)]
+        self._turn = 0
         stream = torch.cuda.Stream(device)
         stream.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(stream):
@@ -481,14 +526,21 @@ class _DecodeGraph:
         torch.cuda.current_stream(device).wait_stream(stream)
 
     def replay(self, tokens: torch.Tensor, positions: Sequence[int]) -> torch.Tensor:
-        self._host_pos.copy_(torch.tensor(list(positions), dtype=torch.int32))
-        self.positions.copy_(self._host_pos, non_blocking=True)
+        host = self._host_pos[self._turn]
+        self._turn ^= 1
+        host.copy_(torch.tensor(list(positions), dtype=torch.int32))
+        self.positions.copy_(host, non_blocking=True)
         self.tokens.copy_(tokens)
         self.graph.replay()
         return self.logits
 
 
 # ------------------------------------------------------------------ helpers
+
+def _decode_ctas(device: torch.device) -> int:
+    """Resident CTAs of the decode kernel on ``device`` (two per SM)."""
+    return 2 * torch.cuda.get_device_properties(device).multi_processor_count
+
 
 def _pack_linears(modules) -> tuple[torch.Tensor, torch.Tensor | None]:
     """Concatenate ``Linear`` weights (and biases) along the output dimension and

@@ -326,14 +326,20 @@ def paged_decode_attention_append(query: torch.Tensor, key: torch.Tensor, value:
     if not slots.is_contiguous():
         slots = slots.contiguous()
     key, value = (t if _rows16(t) else t.contiguous() for t in (key, value))
-    if (query.stride(-1) != 1 or query.stride(0) % 2 or query.stride(1) % 2
+    # With rope the kernel stages the rotated query in `out` with 16-byte vectors.
+    if rope:
+        if not _rows16(query):
+            query = query.contiguous()
+    elif (query.stride(-1) != 1 or query.stride(0) % 2 or query.stride(1) % 2
             or query.data_ptr() % 4):
         query = query.contiguous()
     if out is None:
         out = torch.empty(query.shape, dtype=dtype, device=device)
     elif (out.shape != query.shape or out.dtype != dtype or out.stride(-1) != 1
-          or out.stride(0) % 4 or out.stride(1) % 4 or out.data_ptr() % 8):
-        raise ValueError("out must match the query shape and dtype, with rows 8-byte aligned")
+          or out.stride(0) % 4 or out.stride(1) % 4 or out.data_ptr() % 8
+          or (rope and not _rows16(out))):
+        raise ValueError("out must match the query shape and dtype, with rows 8-byte aligned "
+                         "(16-byte aligned with cos/sin)")
     lib = _lib.load()
     stream = _stream_ptr(device)
     desc = _cache_desc(cache)

@@ -120,3 +120,30 @@ def test_llama_prefix_caching_gives_the_unshared_results():
     assert torch.allclose(shared.prompt_logits, plain.prompt_logits, atol=3e-2, rtol=0)
     _assert_ok(correctness(model, prompts, shared))
     assert shared.cache_released
+
+
+def test_llama_unsynchronised_steps_give_the_same_tokens():
+    """sync_steps=False (the host prepares step N+1 while step N runs, with
+    double-buffered staging) must not change anything the device computes."""
+    model = _model(torch.bfloat16, num_kv_heads=2, num_layers=2, hidden=128, heads=4)
+    prompts = _prompts(6, 21, 128)
+    kwargs = dict(max_new_tokens=6, block_size=8, cuda_graph=True)
+    synced = LlamaPagedDecodeRunner(model, prompts, **kwargs).run()
+    free = LlamaPagedDecodeRunner(model, prompts, sync_steps=False, **kwargs).run()
+    assert free.generated_tokens == synced.generated_tokens
+    for a, b in zip(free.decode_logits, synced.decode_logits):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_llama_fused_and_unfused_decode_agree(fused):
+    """The decode step with the rotary append inside the attention launch and the
+    two-launch step leave identical caches, hence identical tokens and logits."""
+    model = _model(torch.bfloat16, num_kv_heads=2, num_layers=2, hidden=128, heads=4)
+    prompts = _prompts(5, 19, 128)
+    kwargs = dict(max_new_tokens=5, block_size=8, cuda_graph=True)
+    ref = LlamaPagedDecodeRunner(model, prompts, fused_decode=False, **kwargs).run()
+    got = LlamaPagedDecodeRunner(model, prompts, fused_decode=fused, **kwargs).run()
+    assert got.generated_tokens == ref.generated_tokens
+    for a, b in zip(got.decode_logits, ref.decode_logits):
+        assert torch.allclose(a, b, atol=1e-5, rtol=0)
