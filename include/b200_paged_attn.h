@@ -219,11 +219,12 @@ B200_API int b200_rope_append_kv(const b200_cache_desc* cache, const b200_rope_a
  * b200_tc_selftest: one CTA checks the tcgen05 building blocks of the prefill
  * kernel (128-byte swizzled K-major / MN-major shared-memory descriptors,
  * kind::f16 MMAs into tensor memory, tcgen05.ld readback):
- *   c1[128, 64]  = a[128, 64] . b[64, 64]^T,   c2[128, 128] = a[128, 64] . v[64, 128]
- * a, b, v row-major 16-bit (dtype), 16-byte aligned; c1, c2 row-major float32.
+ *   c1[128, 64]  = a[128, 64] . b[64, 64]^T,   c2[128, 128] = a[128, 64] . v[64, 128],
+ *   c3 = c2 with a read from tensor memory (the A-in-TMEM MMA form)
+ * a, b, v row-major 16-bit (dtype), 16-byte aligned; c1, c2, c3 row-major float32.
  * No counterpart in the reference. */
 B200_API int b200_tc_selftest(const void* a, const void* b, const void* v, float* c1, float* c2,
-                              int32_t dtype, uint32_t* error_word, void* stream);
+                              float* c3, int32_t dtype, uint32_t* error_word, void* stream);
 
 /* ------------------------------------------------- decoder-layer helpers
  * Kernels for the Llama layer around the attention call (the reference's

@@ -164,7 +164,7 @@ _PROTOTYPES = {
     "b200_add_rmsnorm": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                         _i64, ctypes.c_float, _i32, _vp]),
     "b200_silu_mul": (ctypes.c_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
-    "b200_tc_selftest": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp]),
+    "b200_tc_selftest": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp]),
     "b200_paged_prefill": (ctypes.c_int, [ctypes.POINTER(CacheDesc), ctypes.POINTER(PrefillArgs),
                                           _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_build_slot_mapping": (ctypes.c_int, [_vp, _i32, _i64, _i32, _vp, _vp, _i32, _i32, _i32,

@@ -18,7 +18,7 @@
 namespace b200 {
 const char* last_error_cstr();
 int launch_tc_selftest(const void* a, const void* b, const void* v, float* c1, float* c2,
-                       int32_t dtype, uint32_t* err, cudaStream_t stream);
+                       float* c3, int32_t dtype, uint32_t* err, cudaStream_t stream);
 }
 
 namespace {
@@ -104,9 +104,9 @@ int b200_rope_append_kv(const b200_cache_desc* cache, const b200_rope_append_arg
 }
 
 int b200_tc_selftest(const void* a, const void* b, const void* v, float* c1, float* c2,
-                     int32_t dtype, uint32_t* error_word, void* stream) {
+                     float* c3, int32_t dtype, uint32_t* error_word, void* stream) {
   return guarded([&] {
-    return b200::launch_tc_selftest(a, b, v, c1, c2, dtype, error_word, as_stream(stream));
+    return b200::launch_tc_selftest(a, b, v, c1, c2, c3, dtype, error_word, as_stream(stream));
   });
 }
 

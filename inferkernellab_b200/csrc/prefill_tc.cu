@@ -15,13 +15,16 @@
 //                      tcgen05.ld, applies the causal / validity mask and a
 //                      base-2 online softmax, rescales its O row in TMEM when
 //                      its running max grew by more than 2^8 (lazy rescale),
-//                      and writes its P row (16-bit) into shared memory as the
-//                      K-major A operand of the P V MMA.  At the end it reads
-//                      its O row, divides by the row sum and stores it.
+//                      and writes its P row (16-bit, tcgen05.st) over the first
+//                      32 columns of the S buffer it just read: the P V MMA
+//                      takes A from tensor memory.  At the end it reads its O
+//                      row, divides by the row sum and stores it.
 //
-// Operand layouts (tcgen05.cuh): Q and P are K-major SW128 (written by the
-// softmax threads), K is K-major SW128 and V is MN-major SW128 as TMA writes
-// them.  Key rows a tile does not hold (past the context, or pages with an
+// Operand layouts (tcgen05.cuh): Q is K-major SW128 (written by the softmax
+// threads), K is K-major SW128 and V is MN-major SW128 as TMA writes them, P is
+// in TMEM.  Shared memory is Q + two K/V stages (D = 128) or three (D = 64),
+// about 100 KB, so two CTAs share an SM and one's softmax overlaps the other's
+// MMAs; TMEM is 256 columns per CTA (S0 | S1 | O), two CTAs fill the SM's 512.  Key rows a tile does not hold (past the context, or pages with an
 // invalid block id) are masked in S and their V rows are zeroed before the
 // P V MMA, so stale or NaN bytes never reach O -- the reference's masked_fill
 // of V (src/inferkernellab/attention.py:301-305).  Semantics are those of the
@@ -31,6 +34,8 @@
 // flag, records the error bit, waits (bounded) for its own MMAs and TMA copies
 // to finish and frees its TMEM before it exits.
 #include <math.h>
+
+#include <algorithm>
 
 #include "../../include/b200_paged_attn.h"
 #include "attn_core.cuh"
@@ -56,14 +61,13 @@ struct TcShape {
   static constexpr int kRegions = D / 64;               // 128-byte column regions
   static constexpr int kTileBytes = kKvTile * D * 2;    // K (or V) of one 64-token tile
   static constexpr int kQBytes = kTcRows * D * 2;       // 128 query rows
-  static constexpr int kPBytes = kTcRows * kKvTile * 2;  // 128 x 64 probabilities
-  static constexpr int kStages = 3;
+  static constexpr int kStages = D >= 128 ? 2 : 3;
   static constexpr int kQRegionBytes = kTcRows * 128;    // 16 KB
   static constexpr int kKvRegionBytes = kKvTile * 128;   // 8 KB
 };
 
 struct TcSmem {
-  int stages_off, q_off, p_off, bars_off, mask_off, flags_off, table_off, begin_off, total;
+  int stages_off, q_off, bars_off, mask_off, flags_off, table_off, begin_off, total;
 };
 
 template <int D>
@@ -75,8 +79,6 @@ __host__ __device__ inline TcSmem tc_smem_layout(int num_seqs, int packed) {
   off += S::kStages * 2 * S::kTileBytes;
   L.q_off = off;
   off += S::kQBytes;
-  L.p_off = off;
-  off += S::kPBytes;
   L.bars_off = off;
   off += (2 * S::kStages + 8) * 8;  // full, empty, s_full[2], s_free[2], p_full, o_done, q_full, idle
   L.mask_off = off;
@@ -92,7 +94,7 @@ __host__ __device__ inline TcSmem tc_smem_layout(int num_seqs, int packed) {
 }
 
 template <typename E, int D>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, 2)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
   using S = TcShape<D>;
@@ -103,7 +105,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   const TcSmem L = tc_smem_layout<D>(p.num_seqs, p.packed);
   uint8_t* q_s = smem + L.q_off;
-  uint8_t* p_s = smem + L.p_off;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bars_off);
   uint64_t* empty_bar = full_bar + kStages;
   uint64_t* s_full = empty_bar + kStages;
@@ -235,7 +236,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint32_t id_s = tc::idesc_f16(kTcRows, kKvTile, E::kIsBf16, false, false);
       const uint32_t id_o = tc::idesc_f16(kTcRows, D, E::kIsBf16, false, true);
       const uint32_t q0 = smem_u32(q_s);
-      const uint32_t p0 = smem_u32(p_s);
       const uint32_t st0 = smem_u32(smem + L.stages_off);
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag, p.err, kErrWaitFull);
       for (int j = 0; ok && j <= n_ktiles; ++j) {
@@ -245,6 +245,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (ok && j >= 2)
             ok = mbar_wait_bounded(&s_free[j & 1], ((j - 2) >> 1) & 1, abort_flag, p.err,
                                    kErrWaitEmpty);
+          // P_{j-2} lives in this S buffer until P V_{j-2} has read it.
+          if (ok && j >= 2)
+            ok = mbar_wait_bounded(o_done, (j - 2) & 1, abort_flag, p.err, kErrWaitFull);
           if (!ok) break;
           tc::fence_after_sync();
           const uint32_t kb = st0 + s * 2 * S::kTileBytes;
@@ -265,11 +268,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (!ok) break;
           tc::fence_after_sync();
           const uint32_t vb = st0 + s * 2 * S::kTileBytes + S::kTileBytes;
+          const uint32_t p_tmem = tmem + (jj & 1) * kKvTile;  // P_jj over S_jj's columns
 #pragma unroll
           for (int k = 0; k < kKvTile / 16; ++k)
-            tc::mma_f16(tmem + kTcOCol, tc::sdesc_sw128(p0 + k * 32, 16, 1024),
-                        tc::sdesc_sw128(vb + k * 2048, S::kKvRegionBytes, 1024), id_o,
-                        jj > 0 || k > 0);
+            tc::mma_f16_tmem_a(tmem + kTcOCol, p_tmem + k * 8,
+                               tc::sdesc_sw128(vb + k * 2048, S::kKvRegionBytes, 1024), id_o,
+                               jj > 0 || k > 0);
           tc::commit(o_done);
           tc::commit(&empty_bar[s]);
         }
@@ -380,17 +384,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(vrow)[c] = make_uint4(0, 0, 0, 0);
         }
       }
-      // P row -> shared memory (K-major SW128).
+      // P row -> the first 32 columns of this tile's S buffer (A operand in TMEM).
+      {
+        uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 v;
-        v.x = pack2<E>(x[8 * c + 0], x[8 * c + 1]);
-        v.y = pack2<E>(x[8 * c + 2], x[8 * c + 3]);
-        v.z = pack2<E>(x[8 * c + 4], x[8 * c + 5]);
-        v.w = pack2<E>(x[8 * c + 6], x[8 * c + 7]);
-        *reinterpret_cast<uint4*>(p_s + tc::sw128_offset(r, c)) = v;
+        for (int c = 0; c < 32; ++c) pk[c] = pack2<E>(x[2 * c], x[2 * c + 1]);
+        tc::st32(lane_base + (j & 1) * kKvTile, pk);
+        tc::wait_st();
       }
-      tc::fence_proxy_async_smem();
+      tc::fence_proxy_async_smem();  // zeroed V rows (generic stores) -> the MMA
       tc::fence_before_sync();
       mbar_arrive(p_full);
     }
@@ -436,7 +438,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 template <typename E, int D>
 int launch_tc_t(const CUtensorMap& kmap, const CUtensorMap& vmap, const PrefillParams& p,
                 dim3 grid, cudaStream_t stream) {
-  const int smem = tc_smem_layout<D>(p.num_seqs, p.packed).total + 1024;
+  // At least 76 KB, so that no more than two CTAs (2 x 256 TMEM columns) share an SM.
+  const int smem = std::max(tc_smem_layout<D>(p.num_seqs, p.packed).total + 1024, 76 * 1024);
   auto kern = paged_prefill_tc_kernel<E, D>;
   static int configured[64] = {0};
   int dev = 0;

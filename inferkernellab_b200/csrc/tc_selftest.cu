@@ -4,9 +4,12 @@
 //
 //   C1[128, 64]  = A[128, 64] . B[64, 64]^T      (A, B K-major)
 //   C2[128, 128] = A[128, 64] . V[64, 128]        (V row-major = MN-major B)
+//   C3[128, 128] = same product with A read from tensor memory (the form the
+//                  prefill kernel uses for P), A written there with tcgen05.st
 //
-// Operands are written to shared memory by threads with the 128-byte swizzle
-// pattern TMA produces.  One CTA of 128 threads.
+// Shared-memory operands are written by threads with the 128-byte swizzle
+// pattern TMA produces.  One CTA of 128 threads; TMEM columns: C1 [0,64),
+// A [64,96), C2 [128,256), C3 [256,384).
 #include "../../include/b200_paged_attn.h"
 #include "common.cuh"
 #include "host_common.h"
@@ -19,7 +22,7 @@ namespace {
 template <typename E>
 __global__ void __launch_bounds__(128) tc_selftest_kernel(const uint16_t* a, const uint16_t* b,
                                                           const uint16_t* v, float* c1, float* c2,
-                                                          uint32_t* err) {
+                                                          float* c3, uint32_t* err) {
   __shared__ __align__(1024) uint8_t sa[128 * 128];
   __shared__ __align__(1024) uint8_t sb[64 * 128];
   __shared__ __align__(1024) uint8_t sv[2 * 64 * 128];
@@ -55,13 +58,25 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const uint16_t* a, con
   }
   tc::fence_proxy_async_smem();
   if (warp == 0) {
-    tc::tmem_alloc(&tmem_base, 256);
+    tc::tmem_alloc(&tmem_base, 512);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
+  const uint32_t lane_addr = tbase + (static_cast<uint32_t>(warp * 32) << 16);
+  {  // A row `tid` -> TMEM columns [64, 96) of lane `tid`
+    uint32_t r[32];
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(a + tid * 64);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) r[j] = src[j];
+    tc::st32(lane_addr + 64, r);
+    tc::wait_st();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
 
   if (tid == 0) {
     const bool bf16 = E::kIsBf16;
@@ -76,6 +91,10 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const uint16_t* a, con
     for (int k = 0; k < 4; ++k)
       tc::mma_f16(tbase + 128, tc::sdesc_sw128(a0 + 32 * k, 16, 1024),
                   tc::sdesc_sw128(v0 + 2048 * k, 8192, 1024), id2, k > 0);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      tc::mma_f16_tmem_a(tbase + 256, tbase + 64 + 8 * k,
+                         tc::sdesc_sw128(v0 + 2048 * k, 8192, 1024), id2, k > 0);
     tc::commit(&bar);
   }
   const bool ok = mbar_wait_bounded(&bar, 0, reinterpret_cast<volatile int*>(&abort_flag), err,
@@ -83,7 +102,6 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const uint16_t* a, con
   tc::fence_after_sync();
   if (ok) {
     const int row = warp * 32 + (tid & 31);
-    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(warp * 32) << 16);
     uint32_t r[32];
 #pragma unroll
     for (int cb = 0; cb < 2; ++cb) {
@@ -99,17 +117,24 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const uint16_t* a, con
 #pragma unroll
       for (int j = 0; j < 32; ++j) c2[row * 128 + cb * 32 + j] = __uint_as_float(r[j]);
     }
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+      tc::ld32(lane_addr + 256 + cb * 32, r);
+      tc::wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) c3[row * 128 + cb * 32 + j] = __uint_as_float(r[j]);
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tbase, 256);
+  if (warp == 0) tc::tmem_dealloc(tbase, 512);
 }
 
 }  // namespace
 
 int launch_tc_selftest(const void* a, const void* b, const void* v, float* c1, float* c2,
-                       int32_t dtype, uint32_t* err, cudaStream_t stream) {
-  if (!a || !b || !v || !c1 || !c2) return set_error(B200_ERR_INVALID, "null pointer");
+                       float* c3, int32_t dtype, uint32_t* err, cudaStream_t stream) {
+  if (!a || !b || !v || !c1 || !c2 || !c3) return set_error(B200_ERR_INVALID, "null pointer");
   if (((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
         reinterpret_cast<uintptr_t>(v)) & 15) != 0)
     return set_error(B200_ERR_INVALID, "operands must be 16-byte aligned");
@@ -117,9 +142,9 @@ int launch_tc_selftest(const void* a, const void* b, const void* v, float* c1, f
   const uint16_t* pb = static_cast<const uint16_t*>(b);
   const uint16_t* pv = static_cast<const uint16_t*>(v);
   if (dtype == B200_BF16)
-    tc_selftest_kernel<BF16><<<1, 128, 0, stream>>>(pa, pb, pv, c1, c2, err);
+    tc_selftest_kernel<BF16><<<1, 128, 0, stream>>>(pa, pb, pv, c1, c2, c3, err);
   else if (dtype == B200_F16)
-    tc_selftest_kernel<Half><<<1, 128, 0, stream>>>(pa, pb, pv, c1, c2, err);
+    tc_selftest_kernel<Half><<<1, 128, 0, stream>>>(pa, pb, pv, c1, c2, c3, err);
   else
     return set_error(B200_ERR_UNSUPPORTED, "dtype must be float16 or bfloat16");
   return cuda_status(cudaGetLastError(), "tc_selftest_kernel launch");

@@ -27,17 +27,19 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
 def test_tcgen05_selftest_descriptors_and_tmem(dtype):
-    """K-major and MN-major 128B-swizzled operands, MMAs into TMEM, tcgen05.ld."""
+    """K-major and MN-major 128B-swizzled operands, MMAs into TMEM, tcgen05.ld, and
+    the A-from-tensor-memory MMA form with A written by tcgen05.st."""
     gen = torch.Generator().manual_seed(3)
     a = torch.randn(128, 64, generator=gen).to(dtype).cuda()
     b = torch.randn(64, 64, generator=gen).to(dtype).cuda()
     v = torch.randn(64, 128, generator=gen).to(dtype).cuda()
     c1 = torch.full((128, 64), float("nan"), device="cuda")
     c2 = torch.full((128, 128), float("nan"), device="cuda")
+    c3 = torch.full((128, 128), float("nan"), device="cuda")
     err = torch.zeros(4, dtype=torch.int32, device="cuda")
     code = _lib.B200_BF16 if dtype == torch.bfloat16 else _lib.B200_F16
     rc = _lib.load().b200_tc_selftest(a.data_ptr(), b.data_ptr(), v.data_ptr(), c1.data_ptr(),
-                                      c2.data_ptr(), code, err.data_ptr(),
+                                      c2.data_ptr(), c3.data_ptr(), code, err.data_ptr(),
                                       ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == _lib.B200_OK, _lib.last_error()
     torch.cuda.synchronize()
@@ -46,6 +48,7 @@ def test_tcgen05_selftest_descriptors_and_tmem(dtype):
     want2 = a.double() @ v.double()
     assert torch.allclose(c1.double(), want1, atol=1e-3, rtol=1e-4)
     assert torch.allclose(c2.double(), want2, atol=1e-3, rtol=1e-4)
+    assert torch.allclose(c3.double(), want2, atol=1e-3, rtol=1e-4)  # A from tensor memory
 
 
 CASES = [
