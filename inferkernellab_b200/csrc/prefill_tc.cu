@@ -80,7 +80,8 @@ __host__ __device__ inline TcSmem tc_smem_layout(int num_seqs, int packed) {
   L.q_off = off;
   off += S::kQBytes;
   L.bars_off = off;
-  off += (2 * S::kStages + 8) * 8;  // full, empty, s_full[2], s_free[2], p_full, o_done, q_full, idle
+  off += (2 * S::kStages + 10) * 8;  // full, empty, s_full[2], s_free[2], p_full, o_done, q_full,
+                                     // idle, pv_done[2]
   L.mask_off = off;
   off += S::kStages * 8;
   L.flags_off = off;
@@ -113,6 +114,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint64_t* o_done = p_full + 1;
   uint64_t* q_full = o_done + 1;
   uint64_t* mma_idle = q_full + 1;
+  uint64_t* pv_done = mma_idle + 1;  // [2]: P V of a tile in S buffer (tile & 1) finished
   uint64_t* stage_mask = reinterpret_cast<uint64_t*>(smem + L.mask_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.flags_off);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.flags_off + 4);
@@ -141,6 +143,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     mbar_init(o_done, 1);
     mbar_init(q_full, kTcSoftmaxWarps * 32);
     mbar_init(mma_idle, 1);
+    mbar_init(&pv_done[0], 1);
+    mbar_init(&pv_done[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -238,44 +242,60 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       const uint32_t q0 = smem_u32(q_s);
       const uint32_t st0 = smem_u32(smem + L.stages_off);
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag, p.err, kErrWaitFull);
-      for (int j = 0; ok && j <= n_ktiles; ++j) {
-        if (j < n_ktiles) {
-          const int s = j % kStages;
-          ok = mbar_wait_bounded(&full_bar[s], (j / kStages) & 1, abort_flag, p.err, kErrWaitFull);
-          if (ok && j >= 2)
-            ok = mbar_wait_bounded(&s_free[j & 1], ((j - 2) >> 1) & 1, abort_flag, p.err,
-                                   kErrWaitEmpty);
-          // P_{j-2} lives in this S buffer until P V_{j-2} has read it.
-          if (ok && j >= 2)
-            ok = mbar_wait_bounded(o_done, (j - 2) & 1, abort_flag, p.err, kErrWaitFull);
-          if (!ok) break;
+      // Issue whichever is ready first: S_ns (K tile landed, its S buffer free:
+      // the softmax has read S_{ns-2} and P V_{ns-2} has consumed P_{ns-2}) or
+      // P V_np (its probabilities are written).  Every barrier probed here has
+      // at most one phase outstanding, so the parity probes cannot alias.
+      int ns = 0, np = 0;  // next S tile, next P V tile
+      unsigned long long last = global_timer_ns();
+      while (ok && np < n_ktiles) {
+        bool progressed = false;
+        if (np < ns && mbar_test_wait(p_full, np & 1)) {
           tc::fence_after_sync();
-          const uint32_t kb = st0 + s * 2 * S::kTileBytes;
-          const uint32_t d_s = tmem + (j & 1) * kKvTile;
-#pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint32_t reg = static_cast<uint32_t>(k >> 2), kk = static_cast<uint32_t>(k & 3);
-            tc::mma_f16(d_s, tc::sdesc_sw128(q0 + reg * S::kQRegionBytes + kk * 32, 16, 1024),
-                        tc::sdesc_sw128(kb + reg * S::kKvRegionBytes + kk * 32, 16, 1024), id_s,
-                        k > 0);
-          }
-          tc::commit(&s_full[j & 1]);
-        }
-        if (j >= 1) {
-          const int jj = j - 1;
-          const int s = jj % kStages;
-          ok = mbar_wait_bounded(p_full, jj & 1, abort_flag, p.err, kErrWaitFull);
-          if (!ok) break;
-          tc::fence_after_sync();
+          const int s = np % kStages;
           const uint32_t vb = st0 + s * 2 * S::kTileBytes + S::kTileBytes;
-          const uint32_t p_tmem = tmem + (jj & 1) * kKvTile;  // P_jj over S_jj's columns
+          const uint32_t p_tmem = tmem + (np & 1) * kKvTile;  // P_np over S_np's columns
 #pragma unroll
           for (int k = 0; k < kKvTile / 16; ++k)
             tc::mma_f16_tmem_a(tmem + kTcOCol, p_tmem + k * 8,
                                tc::sdesc_sw128(vb + k * 2048, S::kKvRegionBytes, 1024), id_o,
-                               jj > 0 || k > 0);
+                               np > 0 || k > 0);
           tc::commit(o_done);
+          tc::commit(&pv_done[np & 1]);
           tc::commit(&empty_bar[s]);
+          ++np;
+          progressed = true;
+        }
+        if (ns < n_ktiles && ns <= np + 1) {
+          const int s = ns % kStages;
+          const bool ready =
+              mbar_test_wait(&full_bar[s], (ns / kStages) & 1) &&
+              (ns < 2 || (mbar_test_wait(&s_free[ns & 1], ((ns - 2) >> 1) & 1) &&
+                          mbar_test_wait(&pv_done[ns & 1], ((ns - 2) >> 1) & 1)));
+          if (ready) {
+            tc::fence_after_sync();
+            const uint32_t kb = st0 + s * 2 * S::kTileBytes;
+            const uint32_t d_s = tmem + (ns & 1) * kKvTile;
+#pragma unroll
+            for (int k = 0; k < D / 16; ++k) {
+              const uint32_t reg = static_cast<uint32_t>(k >> 2), kk = static_cast<uint32_t>(k & 3);
+              tc::mma_f16(d_s, tc::sdesc_sw128(q0 + reg * S::kQRegionBytes + kk * 32, 16, 1024),
+                          tc::sdesc_sw128(kb + reg * S::kKvRegionBytes + kk * 32, 16, 1024), id_s,
+                          k > 0);
+            }
+            tc::commit(&s_full[ns & 1]);
+            ++ns;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          last = global_timer_ns();
+        } else if (*abort_flag) {
+          ok = false;
+        } else if (global_timer_ns() - last > kWaitLimitNs) {
+          *abort_flag = 1;
+          if (p.err) atomicOr(p.err, kErrWaitFull);
+          ok = false;
         }
       }
       // Every MMA this thread issued has finished before TMEM can be freed.
@@ -329,14 +349,22 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 
       const uint64_t tmask = stage_mask[s];
       const int key0 = j * kKvTile;
+      // Keys [key0, key0 + nv) are visible to this row (causal / context limit);
+      // the page-validity bits only matter on tiles with holes (tile-uniform).
+      const int nv = min(max(lim - key0, 0), kKvTile);
+      const uint32_t mlo = static_cast<uint32_t>(tmask);
+      const uint32_t mhi = static_cast<uint32_t>(tmask >> 32);
+      const bool holes = (mlo & mhi) != 0xffffffffu;
       float x[kKvTile];
-      float mx = -INFINITY;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
 #pragma unroll
       for (int c = 0; c < kKvTile; ++c) {
-        const bool valid = ((tmask >> c) & 1ull) && (key0 + c < lim);
+        bool valid = c < nv;
+        if (holes) valid = valid && (((c < 32 ? mlo : mhi) >> (c & 31)) & 1u);
         x[c] = valid ? __uint_as_float(sr[c]) * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, x[c]);
+        mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
       }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       float alpha = 1.f;
       bool rescale = false;
       if (mx != -INFINITY && (m_used == -INFINITY || mx > m_used + kLazyRescale)) {
@@ -346,13 +374,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         }
         m_used = mx;
       }
-      float psum = 0.f;
+      float ps4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < kKvTile; ++c) {
         x[c] = x[c] == -INFINITY ? 0.f : fast_exp2(x[c] - m_used);
-        psum += x[c];
+        ps4[c & 3] += x[c];
       }
-      l_sum = l_sum * alpha + psum;
+      l_sum = l_sum * alpha + ((ps4[0] + ps4[1]) + (ps4[2] + ps4[3]));
 
       // P V of the previous tile must be done before O is rescaled or P rewritten.
       if (j > 0) {
