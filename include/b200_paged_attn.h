@@ -89,9 +89,10 @@ typedef struct {
  * Workspace: `workspace` must hold b200_paged_decode_workspace_bytes() bytes
  * and be ZERO-FILLED before its first use; every launch that completes leaves
  * its split counters at zero again.  The counters sit after the split partials,
- * whose size depends only on (num_q_heads / num_kv_heads, head_dim, dtype), so
- * one workspace can serve any batch size without re-zeroing; re-zero it when
- * the head grouping, head_dim or dtype changes, or after a device error.
+ * whose size depends only on (num_q_heads / num_kv_heads, num_kv_heads,
+ * head_dim, block_size, dtype) -- the last four choose how many KV heads share
+ * one tile -- so one workspace can serve any batch size without re-zeroing;
+ * re-zero it when any of these changes, or after a device error.
  * Calls that share one workspace must be ordered (same stream, or synchronised).
  */
 typedef struct {

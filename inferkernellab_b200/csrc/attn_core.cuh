@@ -146,6 +146,43 @@ __device__ __forceinline__ void issue_kv_tile(const CUtensorMap* kmap, const CUt
   }
 }
 
+// Producer (whole warp), head-group tiles: tokens tok0 .. tok0+ntok-1 (ntok <=
+// tokens = 64 / heads, tok0 a multiple of `tokens`, so one page holds them all)
+// of kv heads head0 .. head0+heads-1, one 4-D TMA box per tensor (the map of a
+// head-group geometry).  Shared memory receives D / 64 regions of 64 rows x
+// 128 bytes, row = head * tokens + token -- the layout issue_kv_tile produces
+// for one head and 64 tokens, so the consumers read both alike.  The validity
+// mask repeats the token bits once per head.
+__device__ __forceinline__ void issue_kv_tile_heads(const CUtensorMap* kmap, const CUtensorMap* vmap,
+                                                    const PagedSource& src, TableWindow& win,
+                                                    int row, int row_pages, int head0, int heads,
+                                                    int tok0, int ntok, uint32_t box_bytes,
+                                                    uint8_t* kdst, uint8_t* vdst, uint64_t* bar,
+                                                    uint64_t* mask_out, uint32_t* err, int lane) {
+  const int tokens = kKvTile / heads;
+  const int page = tok0 / src.block_size;
+  if (win.row != row || page < win.first || page >= win.first + win.count)
+    table_window_refill(win, src, row, page, row_pages, err, lane);
+  if (lane == 0) {
+    const int blk = win.ids[page - win.first];
+    uint64_t m = 0;
+    if (blk >= 0) {
+      const uint64_t span = (1ull << ntok) - 1ull;  // ntok <= 32
+      for (int h = 0; h < heads; ++h) m |= span << (h * tokens);
+    }
+    *mask_out = m;
+    mbar_arrive_expect_tx(bar, blk >= 0 ? 2u * box_bytes : 0u);
+    if (blk >= 0) {
+      const int z = static_cast<int>(src.layer_slot_base +
+                                     static_cast<long long>(blk) * src.block_size +
+                                     (tok0 & (src.block_size - 1)));
+      tma_load_4d(kdst, kmap, bar, 0, z, head0, 0);
+      tma_load_4d(vdst, vmap, bar, 0, z, head0, 0);
+    }
+  }
+  __syncwarp();
+}
+
 // Exclusive prefix sum over the threads of a block of kThreads (a multiple of
 // 32): returns the sum of `v` over lower thread ids; *total gets the block sum.
 // `warp_tot` is shared scratch of kThreads / 32 ints.  Contains __syncthreads.

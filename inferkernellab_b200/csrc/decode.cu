@@ -1,9 +1,11 @@
 // Paged decode attention for sm_100a: split-KV over a persistent stream-K grid.
 //
 // Work decomposition
-//   A *segment* is one (request r, kv head h) pair; it owns ceil(len_r / 64)
-//   *tiles* of 64 logical tokens.  All segments are laid end to end (request
-//   major, then kv head) and the resulting tile range is cut into gridDim.x
+//   A *segment* is one (request r, group of HB kv heads) pair; it owns
+//   ceil(len_r / T) *tiles* of T = 64 / HB logical tokens x HB heads (64 K and
+//   64 V rows either way).  HB = 1 unless head-group tiles apply (below).  All
+//   segments are laid end to end (request major, then head group) and the
+//   resulting tile range is cut into gridDim.x
 //   equal contiguous pieces, one per CTA ("stream-K").  A CTA therefore walks
 //   whole segments plus at most one partial segment at each end, and every CTA
 //   moves the same number of K/V bytes whatever the context-length spread.
@@ -12,15 +14,26 @@
 //   workspace, and the CTA that arrives last on the segment's counter merges the
 //   partials and resets the counter -- no second kernel, no spin waiting.
 //
+// Head-group tiles (HB = 2 or 4; head_dim 64/128, G * HB <= 16, T <= block
+// size): a tile is one TMA box per tensor -- T tokens of HB heads out of one
+// page, through the 4-D head-group tensor map -- instead of one box per page
+// and 128-byte chunk of a single head.  TMA moves bytes at a rate set largely
+// by the number of boxes; at Hkv = 8, D = 128, block size 16 a tile is two
+// 16 KB boxes instead of sixteen 2 KB ones (a pure streaming probe of the
+// config-3 cache: 6.94 TB/s against 6.34).  The boxes land head-major, so
+// consumer warp w still reads tile rows 16w .. 16w+15.
+//
 // Inside a CTA
 //   warp 4 (producer): reads the block table for each tile and issues TMA tile
-//     loads of the K and V page rows of head h into a STAGES-deep shared-memory
-//     ring (mbarrier full/empty pipeline, bounded waits);
+//     loads of the K and V page rows of the segment's heads into a
+//     STAGES-deep shared-memory ring (mbarrier full/empty pipeline, bounded
+//     waits);
 //   warps 0..3 (consumers): the G = Hq/Hkv query heads of the segment form the
 //     M dimension of mma.sync m16n8k16 tiles (padded to 16 rows per m-tile);
 //     S = Q K^T and O += P V run on the tensor cores with fp32 accumulation and
-//     a base-2 online softmax.  Each consumer warp owns a token slice of every
-//     tile; the slices are merged through shared memory at segment end.
+//     a base-2 online softmax.  Each consumer warp owns 16 rows of every tile
+//     (a token slice of one head); the slices of a head are merged through
+//     shared memory at segment end.
 //
 // Masking (reference triton_ops.py:128-165): tokens at or past the context
 // length, and tokens of pages whose block id is outside [0, num_blocks), get
@@ -59,6 +72,8 @@ struct DecodeParams {
   int num_seqs, num_kv_heads, group, table_width;
   int num_blocks, block_size;
   int box_rows, sw_mask;
+  int heads_per_tile;  // HB: kv heads per tile (1, 2 or 4)
+  int tile_tokens;     // T = 64 / HB tokens per tile
   int table64, lens64;
   float scale_log2;
   // Fused new-token append (b200_paged_decode_append); fuse_append == 0 = off.
@@ -100,8 +115,17 @@ struct DecodeSmem {
 
 constexpr int kMergeChunk = 32;  // split pieces merged per pass
 
+// Rows of one segment's reduction arrays: the transposed variants hold at most
+// 16 query heads per segment (G * HB <= 16), the heads-as-M ones 16 * MT.
+template <int MT>
+constexpr int decode_seg_rows() {
+  return MT < 0 ? 16 : 16 * MT;
+}
+
+// `group` = G, `hb` = kv heads per tile.  The slice reduction arrays hold
+// (slices per head) x (G * hb) rows = kSlices x G whatever hb is.
 template <int D, int MT>
-__host__ __device__ inline DecodeSmem decode_smem_layout(int group, int num_seqs) {
+__host__ __device__ inline DecodeSmem decode_smem_layout(int group, int hb, int num_seqs) {
   using S = DecodeShape<D>;
   constexpr int kSlices = MT < 0 ? kDecConsumerWarps : kDecConsumerWarps / MT;
   constexpr int kRows = MT < 0 ? 8 * -MT : 16 * MT;
@@ -120,13 +144,13 @@ __host__ __device__ inline DecodeSmem decode_smem_layout(int group, int num_seqs
   off += kSlices * kRows * 4;
   L.red_w_off = off;
   off += kSlices * kRows * 4;
-  L.row_off = off;  // base and 1/l (or sum) per row
-  off += 2 * kRows * 4;
+  L.row_off = off;  // base and 1/l (or sum) per segment row
+  off += 2 * decode_seg_rows<MT>() * 4;
   off = (off + 15) & ~15;
   L.red_o_off = off;
   off += kSlices * group * D * 4;
   L.merge_w_off = off;
-  off += kMergeChunk * group * 4;
+  off += kMergeChunk * group * hb * 4;
   L.table_off = off;
   off += kTableWindow * 4;
   L.len_off = off;
@@ -139,31 +163,32 @@ __host__ __device__ inline DecodeSmem decode_smem_layout(int group, int num_seqs
   return L;
 }
 
-// Walks tiles in global order: request-major, then kv head, then tile.
+// Walks tiles in global order: request-major, then head group h (of
+// `groups` = Hkv / HB), then tile t (of nt = ceil(len / tile_tokens)).
 struct TileCursor {
   int r, h, t, nt;
-  __device__ void init(int tile, const int* begin, const int* lens, int num_seqs, int hkv) {
+  __device__ void init(int tile, const int* begin, const int* lens, int num_seqs,
+                       int tile_tokens) {
     int lo = 0, hi = num_seqs;
     while (hi - lo > 1) {
       int mid = (lo + hi) >> 1;
       if (begin[mid] <= tile) lo = mid; else hi = mid;
     }
     r = lo;
-    nt = (lens[r] + kDecTile - 1) / kDecTile;
+    nt = (lens[r] + tile_tokens - 1) / tile_tokens;
     int local = tile - begin[r];
     h = local / nt;
     t = local - h * nt;
-    (void)hkv;
   }
-  __device__ void advance(const int* lens, int num_seqs, int hkv) {
+  __device__ void advance(const int* lens, int num_seqs, int groups, int tile_tokens) {
     if (++t < nt) return;
     t = 0;
-    if (++h < hkv) return;
+    if (++h < groups) return;
     h = 0;
     do {
       ++r;
     } while (r < num_seqs && lens[r] == 0);
-    nt = r < num_seqs ? (lens[r] + kDecTile - 1) / kDecTile : 0;
+    nt = r < num_seqs ? (lens[r] + tile_tokens - 1) / tile_tokens : 0;
   }
 };
 
@@ -214,11 +239,16 @@ __device__ __forceinline__ void fused_prologue(const DecodeParams& p, const int*
   const int kv_items = 2 * kVec;                       // V vectors, then K vectors / pairs
   const int q_items = p.rope ? p.group * kHalf : 0;    // rotary pairs of the G query heads
   const int per_seg = kv_items + q_items;
+  // Segments are (request, head group); an item belongs to one kv head of the
+  // segments this range touches: kv-head unit u = r * hkv + h, and segment g
+  // covers units g * hb .. g * hb + hb - 1.
+  const int hb = p.heads_per_tile;
+  const int groups = hkv / hb;
   TileCursor first, last;
-  first.init(my_begin, begin_s, len_s, p.num_seqs, hkv);
-  last.init(my_end - 1, begin_s, len_s, p.num_seqs, hkv);
-  const int g0 = first.r * hkv + first.h;
-  const int total = (last.r * hkv + last.h - g0 + 1) * per_seg;
+  first.init(my_begin, begin_s, len_s, p.num_seqs, p.tile_tokens);
+  last.init(my_end - 1, begin_s, len_s, p.num_seqs, p.tile_tokens);
+  const int g0 = first.r * groups + first.h;
+  const int total = (last.r * groups + last.h - g0 + 1) * hb * per_seg;
   enum : int { kNone = 0, kV = 1, kK = 2, kQ = 3 };
   for (int base = thread; base < total; base += nthreads * kUnroll) {
     int kind[kUnroll], r_[kUnroll], h_[kUnroll], j_[kUnroll];
@@ -232,9 +262,9 @@ __device__ __forceinline__ void fused_prologue(const DecodeParams& p, const int*
       if (it >= total) continue;
       const int k = it / per_seg;
       const int item = it - k * per_seg;
-      const int g = g0 + k;
-      const int r = g / hkv;
-      const int h = g - r * hkv;
+      const int unit = g0 * hb + k;
+      const int r = unit / hkv;
+      const int h = unit - r * hkv;
       const int len = len_s[r];
       if (len == 0) continue;
       r_[u] = r;
@@ -253,8 +283,8 @@ __device__ __forceinline__ void fused_prologue(const DecodeParams& p, const int*
         head_[u] = head;
         kind[u] = kQ;
       } else {
-        const int nt = (len + kDecTile - 1) / kDecTile;
-        const int last_tile = begin_s[r] + h * nt + nt - 1;
+        const int nt = (len + p.tile_tokens - 1) / p.tile_tokens;
+        const int last_tile = begin_s[r] + (h / hb) * nt + nt - 1;
         if (last_tile < my_begin || last_tile >= my_end) continue;
         if (item < kVec) {
           x0[u] = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.new_v) +
@@ -370,12 +400,13 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   constexpr int kStages = S::kStages;
   constexpr int kConsumers = kDecConsumerWarps * 32;
   constexpr int kD4 = D / 4;
-  constexpr int kElems4 = (kRows * kD4 + kConsumers - 1) / kConsumers;  // float4 per thread
+  constexpr int kElems4 =
+      (decode_seg_rows<MT>() * kD4 + kConsumers - 1) / kConsumers;  // float4 per thread
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  const DecodeSmem L = decode_smem_layout<D, MT>(p.group, p.num_seqs);
+  const DecodeSmem L = decode_smem_layout<D, MT>(p.group, p.heads_per_tile, p.num_seqs);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bars_off);
   uint64_t* empty_bar = full_bar + kStages;
   uint64_t* stage_mask = reinterpret_cast<uint64_t*>(smem + L.mask_off);
@@ -385,7 +416,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   float* red_l = reinterpret_cast<float*>(smem + L.red_l_off);
   float* red_w = reinterpret_cast<float*>(smem + L.red_w_off);
   float* row_base = reinterpret_cast<float*>(smem + L.row_off);
-  float* row_l = row_base + kRows;
+  float* row_l = row_base + decode_seg_rows<MT>();
   float* red_o = reinterpret_cast<float*>(smem + L.red_o_off);
   float* merge_w = reinterpret_cast<float*>(smem + L.merge_w_off);
   int* len_s = reinterpret_cast<int*>(smem + L.len_off);
@@ -398,6 +429,10 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   const int B = p.num_seqs;
   const int HKV = p.num_kv_heads;
   const int G = p.group;
+  const int HB = p.heads_per_tile;  // kv heads per tile
+  const int HG = HKV / HB;          // head groups (segments per request)
+  const int TT = p.tile_tokens;     // tokens per tile
+  const int GH = G * HB;            // query heads per segment
 
   // ---- prologue: effective lengths and the tile prefix over requests ----
   const long long cap = static_cast<long long>(p.table_width) * p.block_size;
@@ -424,12 +459,12 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
     const int lo = min(B, tid * chunk);
     const int hi = min(B, lo + chunk);
     int sum = 0;
-    for (int i = lo; i < hi; ++i) sum += ((len_s[i] + kDecTile - 1) / kDecTile) * HKV;
+    for (int i = lo; i < hi; ++i) sum += ((len_s[i] + TT - 1) / TT) * HG;
     int total_all = 0;
     int acc = block_exclusive_scan<kDecThreads>(sum, scan_s, &total_all);
     for (int i = lo; i < hi; ++i) {
       begin_s[i] = acc;
-      acc += ((len_s[i] + kDecTile - 1) / kDecTile) * HKV;
+      acc += ((len_s[i] + TT - 1) / TT) * HG;
     }
     if (tid == 0) begin_s[B] = total_all;
   }
@@ -492,7 +527,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
     win.first = 0;
     win.count = 0;
     TileCursor cur;
-    cur.init(my_begin, begin_s, len_s, B, HKV);
+    cur.init(my_begin, begin_s, len_s, B, TT);
     int issued = 0;
     bool appended = !FUSED;
     for (int it = 0; it < n_tiles; ++it) {
@@ -505,14 +540,19 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       if (!mbar_wait_bounded(&empty_bar[s], (k & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty))
         break;
       const int len = len_s[cur.r];
-      const int tok0 = cur.t * kDecTile;
-      const int ntok = min(kDecTile, len - tok0);
+      const int tok0 = cur.t * TT;
+      const int ntok = min(TT, len - tok0);
       uint8_t* kdst = smem + s * L.stage_bytes;
-      issue_kv_tile<D>(&kmap, &vmap, src, win, cur.r, (len + p.block_size - 1) / p.block_size,
-                       cur.h, tok0, ntok, kdst, kdst + S::kTileBytes, &full_bar[s],
-                       &stage_mask[s], p.err, lane);
+      const int row_pages = (len + p.block_size - 1) / p.block_size;
+      if (HB > 1)
+        issue_kv_tile_heads(&kmap, &vmap, src, win, cur.r, row_pages, cur.h * HB, HB, tok0, ntok,
+                            S::kTileBytes, kdst, kdst + S::kTileBytes, &full_bar[s],
+                            &stage_mask[s], p.err, lane);
+      else
+        issue_kv_tile<D>(&kmap, &vmap, src, win, cur.r, row_pages, cur.h, tok0, ntok, kdst,
+                         kdst + S::kTileBytes, &full_bar[s], &stage_mask[s], p.err, lane);
       ++issued;
-      cur.advance(len_s, B, HKV);
+      cur.advance(len_s, B, HG, TT);
     }
     if (FUSED && !appended) named_bar_sync(kBarAppended, kDecThreads);
     // Drain: the last phases this warp armed must complete before the CTA
@@ -529,6 +569,13 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   const int row0 = mt * 16 + g;  // heads-as-M: query-head row inside the group
   const int row1 = row0 + 8;
   const uint32_t sw = static_cast<uint32_t>(p.sw_mask);
+  // Transposed variants: warp w reads tile rows 16w..16w+15, i.e. head hl =
+  // w / SPH of the tile's HB heads, token slice w % SPH (SPH = 4 / HB slices per
+  // head).  Heads-as-M variants: HB = 1, kSlices slices of MT warps each.
+  const int SPH = kTrans ? kDecConsumerWarps / HB : kSlices;
+  const int hl = kTrans ? warp / SPH : 0;
+  const int sl_h = kTrans ? warp - hl * SPH : slice;  // slice within the head
+  const int rstride = kTrans ? GH : kRows;            // reduction-array row stride
 
   // heads-as-M state
   uint32_t qf[D / 16][4];
@@ -541,7 +588,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   bool aborted = false;
 
   TileCursor cur;
-  cur.init(my_begin, begin_s, len_s, B, HKV);
+  cur.init(my_begin, begin_s, len_s, B, TT);
   bool seg_start = true;
 
   for (int it = 0; it < n_tiles; ++it) {
@@ -549,10 +596,11 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       seg_start = false;
       // With the fused rotary append, the prologue staged the rotated q in `out`.
       const bool staged = FUSED && p.rope;
+      const long long qhead0 = static_cast<long long>(cur.h * HB + hl) * G;
       const T* qg = staged ? reinterpret_cast<const T*>(p.out) + cur.r * p.out_stride_seq +
-                                 static_cast<long long>(cur.h * G) * p.out_stride_head
+                                 qhead0 * p.out_stride_head
                            : reinterpret_cast<const T*>(p.q) + cur.r * p.q_stride_seq +
-                                 static_cast<long long>(cur.h * G) * p.q_stride_head;
+                                 qhead0 * p.q_stride_head;
       const long long q_head_stride = staged ? p.out_stride_head : p.q_stride_head;
       if constexpr (kTrans) {
         load_qT_frag<E, D, NT>(qb, qg, q_head_stride, G, lane);
@@ -607,13 +655,13 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
     // ---- segment end: merge the token slices, then finish or publish ----
     const bool seg_end = (cur.t == cur.nt - 1) || (it == n_tiles - 1);
     if (seg_end) {
-      const int seg = cur.r * HKV + cur.h;
+      const int seg = cur.r * HG + cur.h;
       const int seg_begin = begin_s[cur.r] + cur.h * cur.nt;
       const int seg_end_tile = seg_begin + cur.nt;
       const bool complete = seg_begin >= my_begin && seg_end_tile <= my_end;
       const int slot = seg_begin <= my_begin ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
       T* out_seg = reinterpret_cast<T*>(p.out) + cur.r * p.out_stride_seq +
-                   static_cast<long long>(cur.h * G) * p.out_stride_head;
+                   static_cast<long long>(cur.h * GH) * p.out_stride_head;
       if constexpr (kTrans) {
         // l: reduce each head's partial over the 8 key lanes (g).
 #pragma unroll
@@ -630,22 +678,27 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             const int h0 = nt * 8 + 2 * tq;
+            const int sr = hl * G + h0;  // segment row of query head h0 of this warp's kv head
             if (g == 0) {
-              red_m[slice * kRows + h0] = m_t[nt][0];
-              red_m[slice * kRows + h0 + 1] = m_t[nt][1];
-              red_l[slice * kRows + h0] = l_t[nt][0];
-              red_l[slice * kRows + h0 + 1] = l_t[nt][1];
+              if (h0 < G) {
+                red_m[sl_h * rstride + sr] = m_t[nt][0];
+                red_l[sl_h * rstride + sr] = l_t[nt][0];
+              }
+              if (h0 + 1 < G) {
+                red_m[sl_h * rstride + sr + 1] = m_t[nt][1];
+                red_l[sl_h * rstride + sr + 1] = l_t[nt][1];
+              }
             }
 #pragma unroll
             for (int i = 0; i < D / 16; ++i) {
               const int d0 = i * 16 + g;
               if (h0 < G) {
-                float* dst = red_o + (slice * G + h0) * D;
+                float* dst = red_o + (sl_h * GH + sr) * D;
                 dst[d0] = oT[nt][i][0];
                 dst[d0 + 8] = oT[nt][i][2];
               }
               if (h0 + 1 < G) {
-                float* dst = red_o + (slice * G + h0 + 1) * D;
+                float* dst = red_o + (sl_h * GH + sr + 1) * D;
                 dst[d0] = oT[nt][i][1];
                 dst[d0 + 8] = oT[nt][i][3];
               }
@@ -677,36 +730,33 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
         }
       }
       named_bar_sync(1, kConsumers);
-      // Per-row slice weights, once per row.
+      // Per-row slice weights, once per row (segment rows = the GH query heads).
       if (!aborted) {
-        for (int row = tid; row < G; row += kConsumers) {
+        for (int row = tid; row < GH; row += kConsumers) {
           float mmax = -INFINITY;
-#pragma unroll
-          for (int sl = 0; sl < kSlices; ++sl) mmax = fmaxf(mmax, red_m[sl * kRows + row]);
+          for (int sl = 0; sl < SPH; ++sl) mmax = fmaxf(mmax, red_m[sl * rstride + row]);
           const float base = mmax == -INFINITY ? 0.f : mmax;
           float lsum = 0.f;
-#pragma unroll
-          for (int sl = 0; sl < kSlices; ++sl) {
-            const float w = fast_exp2(red_m[sl * kRows + row] - base);
-            red_w[sl * kRows + row] = w;
-            lsum += red_l[sl * kRows + row] * w;
+          for (int sl = 0; sl < SPH; ++sl) {
+            const float w = fast_exp2(red_m[sl * rstride + row] - base);
+            red_w[sl * rstride + row] = w;
+            lsum += red_l[sl * rstride + row] * w;
           }
           row_base[row] = base;
           row_l[row] = lsum;
           if (!complete)
-            p.part_lse[slot * G + row] = lsum > 0.f ? base + fast_log2(lsum) : -INFINITY;
+            p.part_lse[slot * GH + row] = lsum > 0.f ? base + fast_log2(lsum) : -INFINITY;
         }
       }
       named_bar_sync(1, kConsumers);
       if (!aborted) {
-        for (int e = tid; e < G * kD4; e += kConsumers) {
+        for (int e = tid; e < GH * kD4; e += kConsumers) {
           const int row = e / kD4;
           const int d4 = e - row * kD4;
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int sl = 0; sl < kSlices; ++sl) {
-            const float w = red_w[sl * kRows + row];
-            const float4 v = reinterpret_cast<const float4*>(red_o + (sl * G + row) * D)[d4];
+          for (int sl = 0; sl < SPH; ++sl) {
+            const float w = red_w[sl * rstride + row];
+            const float4 v = reinterpret_cast<const float4*>(red_o + (sl * GH + row) * D)[d4];
             acc.x += w * v.x;
             acc.y += w * v.y;
             acc.z += w * v.z;
@@ -720,7 +770,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
           if (complete)
             store4<E>(out_seg + row * p.out_stride_head + d4 * 4, acc);
           else
-            reinterpret_cast<float4*>(p.part_o)[(static_cast<long long>(slot) * G + row) * kD4 +
+            reinterpret_cast<float4*>(p.part_o)[(static_cast<long long>(slot) * GH + row) * kD4 +
                                                 d4] = acc;
         }
       }
@@ -750,11 +800,11 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
           // then combined across the warp.  With few pieces the lse values stay
           // in merge_w for the weights below (no second global read).
           const bool lse_cached = npieces <= kMergeChunk;
-          for (int row = warp; row < G; row += kDecConsumerWarps) {
+          for (int row = warp; row < GH; row += kDecConsumerWarps) {
             float m = -INFINITY, sum = 0.f;
             for (int i = lane; i < npieces; i += 32) {
-              const float lse = __ldcg(p.part_lse + piece_slot(i) * G + row);
-              if (lse_cached) merge_w[i * G + row] = lse;
+              const float lse = __ldcg(p.part_lse + piece_slot(i) * GH + row);
+              if (lse_cached) merge_w[i * GH + row] = lse;
               if (lse == -INFINITY) continue;
               if (lse > m) {
                 sum = (m == -INFINITY ? 0.f : sum * fast_exp2(m - lse)) + 1.f;
@@ -785,13 +835,13 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
           for (int k4 = 0; k4 < kElems4; ++k4) acc[k4] = make_float4(0.f, 0.f, 0.f, 0.f);
           for (int c0 = 0; c0 < npieces; c0 += kMergeChunk) {
             const int nq = min(kMergeChunk, npieces - c0);
-            for (int i = tid; i < kMergeChunk * G; i += kConsumers) {
-              const int q = i / G;
-              const int row = i - q * G;
+            for (int i = tid; i < kMergeChunk * GH; i += kConsumers) {
+              const int q = i / GH;
+              const int row = i - q * GH;
               float w = 0.f;
               if (q < nq) {
                 const float lse =
-                    lse_cached ? merge_w[i] : __ldcg(p.part_lse + piece_slot(c0 + q) * G + row);
+                    lse_cached ? merge_w[i] : __ldcg(p.part_lse + piece_slot(c0 + q) * GH + row);
                 if (lse != -INFINITY) w = fast_exp2(lse - row_base[row]) * row_l[row];
               }
               merge_w[i] = w;
@@ -800,15 +850,15 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
 #pragma unroll
             for (int k4 = 0; k4 < kElems4; ++k4) {
               const int e = tid + k4 * kConsumers;
-              if (e < G * kD4) {
+              if (e < GH * kD4) {
                 const int row = e / kD4;
                 const int d4 = e - row * kD4;
 #pragma unroll 4
                 for (int q = 0; q < nq; ++q) {
-                  const float w = merge_w[q * G + row];
+                  const float w = merge_w[q * GH + row];
                   if (w == 0.f) continue;
                   const float4 v = __ldcg(reinterpret_cast<const float4*>(p.part_o) +
-                                          (static_cast<long long>(piece_slot(c0 + q)) * G + row) *
+                                          (static_cast<long long>(piece_slot(c0 + q)) * GH + row) *
                                               kD4 + d4);
                   acc[k4].x += w * v.x;
                   acc[k4].y += w * v.y;
@@ -822,7 +872,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
 #pragma unroll
           for (int k4 = 0; k4 < kElems4; ++k4) {
             const int e = tid + k4 * kConsumers;
-            if (e < G * kD4) {
+            if (e < GH * kD4) {
               const int row = e / kD4;
               store4<E>(out_seg + row * p.out_stride_head + (e - row * kD4) * 4, acc[k4]);
             }
@@ -833,7 +883,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       named_bar_sync(1, kConsumers);
       seg_start = true;
     }
-    cur.advance(len_s, B, HKV);
+    cur.advance(len_s, B, HG, TT);
   }
 }
 
@@ -844,8 +894,9 @@ struct WorkspaceLayout {
 };
 
 // [0, 256): device error word.  Then the split partials, whose size depends only
-// on (grid, group, head_dim) -- fixed for a model on a device -- and last the
-// per-segment counters (num_seqs * kv_heads).  Counters go last so that a change
+// on (grid, query heads per segment = G * HB, head_dim) -- fixed for a model on
+// a device -- and last the per-segment counters (num_seqs * kv_heads, at least
+// the number of segments).  Counters go last so that a change
 // of batch size never moves them onto bytes that held partials: counters past
 // the previous batch were never written, the others were reset by the kernel.
 static WorkspaceLayout workspace_layout(int num_seqs, int hkv, int group, int head_dim, int grid) {
@@ -868,7 +919,7 @@ template <typename E, int D, int MT>
 static int launch_decode_t(const CUtensorMap& kmap, const CUtensorMap& vmap,
                            const DecodeParams& p, int num_sms, int* grid_out, bool dry_run,
                            cudaStream_t stream) {
-  const DecodeSmem L = decode_smem_layout<D, MT>(p.group, p.num_seqs);
+  const DecodeSmem L = decode_smem_layout<D, MT>(p.group, p.heads_per_tile, p.num_seqs);
   const int smem = L.total + 1024;
   const int fused = p.fuse_append ? 1 : 0;
   auto kern = fused ? paged_decode_kernel<E, D, MT, true> : paged_decode_kernel<E, D, MT, false>;
@@ -888,7 +939,7 @@ static int launch_decode_t(const CUtensorMap& kmap, const CUtensorMap& vmap,
   const int grid = num_sms * per_sm;
   // The workspace is sized for the largest grid of this instantiation (the
   // occupancy at batch size 1), so its layout does not move with the batch.
-  const int smem_min = decode_smem_layout<D, MT>(p.group, 1).total + 1024;
+  const int smem_min = decode_smem_layout<D, MT>(p.group, p.heads_per_tile, 1).total + 1024;
   int per_sm_max = 0;
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_max, kern, kDecThreads, smem_min);
   if (err != cudaSuccess) return cuda_status(err, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
@@ -902,6 +953,17 @@ static int launch_decode_t(const CUtensorMap& kmap, const CUtensorMap& vmap,
 // transposed form; 2 (G <= 32) and 4 (G <= 64) put the heads on the M rows.
 static int decode_variant(int group) {
   return group <= 8 ? -1 : (group <= 16 ? -2 : (group <= 32 ? 2 : 4));
+}
+
+// Kv heads per tile: 4 or 2 where the head-group geometry applies (transposed
+// variants, G * HB <= 16 query heads per segment, head_dim 64/128, one page
+// covering 64 / HB tokens), else 1.
+static int decode_heads_per_tile(const b200_cache_desc* c, int group) {
+  if (decode_variant(group) > 0) return 1;
+  CacheTmaGeometry geo;
+  for (int hb = 4; hb >= 2; hb /= 2)
+    if (group * hb <= 16 && cache_head_group_geometry(c, hb, &geo)) return hb;
+  return 1;
 }
 
 template <typename E, int D>
@@ -967,16 +1029,18 @@ size_t decode_workspace_bytes(const b200_cache_desc* c, const b200_decode_args* 
   if (current_device_info(&info) != B200_OK) return 0;
   const int group = a->num_q_heads / c->num_kv_heads;
   const int mt = decode_variant(group);
+  const int hb = decode_heads_per_tile(c, group);
   CUtensorMap dummy;
   DecodeParams p{};
   p.group = group;
+  p.heads_per_tile = hb;
   p.num_seqs = a->num_seqs;
   int grid = 0;
   int rc = c->dtype == B200_BF16
                ? dispatch_d<BF16>(c->head_dim, mt, dummy, dummy, p, info.num_sms, &grid, true, 0)
                : dispatch_d<Half>(c->head_dim, mt, dummy, dummy, p, info.num_sms, &grid, true, 0);
   if (rc != B200_OK) return 0;
-  return workspace_layout(a->num_seqs, c->num_kv_heads, group, c->head_dim, grid).total;
+  return workspace_layout(a->num_seqs, c->num_kv_heads, group * hb, c->head_dim, grid).total;
 }
 
 // Inputs of the fused new-token append (b200_paged_decode_append).
@@ -1026,17 +1090,23 @@ static int launch_decode_common(const b200_cache_desc* c, const b200_decode_args
   DeviceInfo info;
   rc = current_device_info(&info);
   if (rc != B200_OK) return rc;
+  const int group = a->num_q_heads / c->num_kv_heads;
+  const int mt = decode_variant(group);
+  const int hb = decode_heads_per_tile(c, group);
   CacheTmaGeometry geo;
   std::string why;
-  if (!cache_tma_geometry(c, kDecTile, &geo, &why)) return set_error(B200_ERR_UNSUPPORTED, why);
+  if (hb > 1) {
+    if (!cache_head_group_geometry(c, hb, &geo))
+      return set_error(B200_ERR_UNSUPPORTED, "head-group geometry rejected");
+  } else if (!cache_tma_geometry(c, kDecTile, &geo, &why)) {
+    return set_error(B200_ERR_UNSUPPORTED, why);
+  }
   CUtensorMap kmap, vmap;
   rc = encode_cache_tensor_map(c, c->k_cache, geo, &kmap);
   if (rc != B200_OK) return rc;
   rc = encode_cache_tensor_map(c, c->v_cache, geo, &vmap);
   if (rc != B200_OK) return rc;
 
-  const int group = a->num_q_heads / c->num_kv_heads;
-  const int mt = decode_variant(group);
   DecodeParams p{};
   p.q = query;
   p.out = out;
@@ -1056,6 +1126,8 @@ static int launch_decode_common(const b200_cache_desc* c, const b200_decode_args
   p.block_size = c->block_size;
   p.box_rows = geo.box_rows;
   p.sw_mask = geo.swizzle_bytes == 0 ? 0 : geo.swizzle_bytes / 16 - 1;
+  p.heads_per_tile = hb;
+  p.tile_tokens = kDecTile / hb;
   p.table64 = a->table_dtype == B200_I64;
   p.lens64 = a->lens_dtype == B200_I64;
   p.scale_log2 = a->scale * 1.4426950408889634f;
@@ -1084,7 +1156,8 @@ static int launch_decode_common(const b200_cache_desc* c, const b200_decode_args
            ? dispatch_d<BF16>(c->head_dim, mt, kmap, vmap, p, info.num_sms, &grid, true, stream)
            : dispatch_d<Half>(c->head_dim, mt, kmap, vmap, p, info.num_sms, &grid, true, stream);
   if (rc != B200_OK) return rc;
-  const WorkspaceLayout w = workspace_layout(a->num_seqs, c->num_kv_heads, group, c->head_dim, grid);
+  const WorkspaceLayout w =
+      workspace_layout(a->num_seqs, c->num_kv_heads, group * hb, c->head_dim, grid);
   if (workspace == nullptr || workspace_bytes < w.total)
     return set_error(B200_ERR_WORKSPACE, "decode workspace missing or smaller than "
                                          "b200_paged_decode_workspace_bytes()");
@@ -1170,16 +1243,19 @@ int launch_paged_decode_noalloc(const b200_cache_desc* c, const b200_decode_args
   if (rc != B200_OK) return rc;
   const int group = a->num_q_heads / c->num_kv_heads;
   const int mt = decode_variant(group);
+  const int hb = decode_heads_per_tile(c, group);
   CUtensorMap unused;
   DecodeParams probe{};
   probe.group = group;
+  probe.heads_per_tile = hb;
   probe.num_seqs = a->num_seqs;
   int grid = 0;
   rc = c->dtype == B200_BF16
            ? dispatch_d<BF16>(c->head_dim, mt, unused, unused, probe, info.num_sms, &grid, true, stream)
            : dispatch_d<Half>(c->head_dim, mt, unused, unused, probe, info.num_sms, &grid, true, stream);
   if (rc != B200_OK) return rc;
-  const WorkspaceLayout w = workspace_layout(a->num_seqs, c->num_kv_heads, group, c->head_dim, grid);
+  const WorkspaceLayout w =
+      workspace_layout(a->num_seqs, c->num_kv_heads, group * hb, c->head_dim, grid);
   if (w.total > kDecodeNoAllocScratchBytes)
     return set_error(B200_ERR_WORKSPACE,
                      "this decode shape needs " + std::to_string(w.total) +

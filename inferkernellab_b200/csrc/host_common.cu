@@ -21,10 +21,11 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 struct MapKey {
   const void* base;
   int64_t slots;
-  int heads, dim, dtype, chunk, rows, swz;
+  int heads, dim, dtype, chunk, rows, swz, box_heads;
   bool operator==(const MapKey& o) const {
     return base == o.base && slots == o.slots && heads == o.heads && dim == o.dim &&
-           dtype == o.dtype && chunk == o.chunk && rows == o.rows && swz == o.swz;
+           dtype == o.dtype && chunk == o.chunk && rows == o.rows && swz == o.swz &&
+           box_heads == o.box_heads;
   }
 };
 struct MapKeyHash {
@@ -32,7 +33,7 @@ struct MapKeyHash {
     size_t h = std::hash<const void*>()(k.base);
     h ^= std::hash<int64_t>()(k.slots) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
     h ^= static_cast<size_t>(k.heads * 131 + k.dim * 7 + k.dtype + k.chunk * 31 + k.rows * 17 +
-                             k.swz * 3);
+                             k.swz * 3 + k.box_heads * 1009);
     return h;
   }
 };
@@ -90,6 +91,22 @@ bool cache_tma_geometry(const b200_cache_desc* c, int tile_tokens, CacheTmaGeome
   // Swizzle only when every box starts on a swizzle-atom (1024-byte) boundary
   // so the pattern seen by the reader is the same however TMA anchors it.
   geo->swizzle_bytes = (box_bytes % 1024 == 0) ? geo->chunk_bytes : 0;
+  geo->heads_per_box = 1;
+  return true;
+}
+
+bool cache_head_group_geometry(const b200_cache_desc* c, int heads, CacheTmaGeometry* geo) {
+  if (heads != 2 && heads != 4) return false;
+  if (c->head_dim != 64 && c->head_dim != 128) return false;
+  if (c->num_kv_heads % heads != 0) return false;
+  const int tokens = 64 / heads;
+  if (c->block_size < tokens) return false;  // one page must cover the tile
+  geo->chunk_bytes = 128;
+  geo->chunk_elems = 64;
+  geo->num_chunks = c->head_dim / 64;
+  geo->box_rows = tokens;
+  geo->swizzle_bytes = 128;  // each region is 64 rows x 128 bytes, 1024-byte aligned
+  geo->heads_per_box = heads;
   return true;
 }
 
@@ -98,7 +115,7 @@ int encode_cache_tensor_map(const b200_cache_desc* c, const void* base,
   const int64_t slots =
       static_cast<int64_t>(c->num_layers) * c->num_blocks * static_cast<int64_t>(c->block_size);
   MapKey key{base, slots, c->num_kv_heads, c->head_dim, c->dtype, geo.chunk_elems,
-             geo.box_rows, geo.swizzle_bytes};
+             geo.box_rows, geo.swizzle_bytes, geo.heads_per_box};
   std::lock_guard<std::mutex> lock(g_mu);
   auto it = g_maps.find(key);
   if (it != g_maps.end()) {
@@ -126,14 +143,30 @@ int encode_cache_tensor_map(const b200_cache_desc* c, const void* base,
   if (geo.swizzle_bytes == 32) swz = CU_TENSOR_MAP_SWIZZLE_32B;
   if (geo.swizzle_bytes == 64) swz = CU_TENSOR_MAP_SWIZZLE_64B;
   if (geo.swizzle_bytes == 128) swz = CU_TENSOR_MAP_SWIZZLE_128B;
+  // Head-group view: dims {chunk elems, token slot, kv head, chunk}; the strides
+  // are not in increasing order (row, then head, then chunk bytes), which is
+  // what makes the box land head-major in shared memory.
+  cuuint64_t gdim4[4] = {static_cast<cuuint64_t>(geo.chunk_elems), static_cast<cuuint64_t>(slots),
+                         static_cast<cuuint64_t>(c->num_kv_heads),
+                         static_cast<cuuint64_t>(geo.num_chunks)};
+  cuuint64_t gstride4[3] = {static_cast<cuuint64_t>(c->num_kv_heads) * c->head_dim * 2,
+                            static_cast<cuuint64_t>(c->head_dim) * 2,
+                            static_cast<cuuint64_t>(geo.chunk_bytes)};
+  cuuint32_t box4[4] = {static_cast<cuuint32_t>(geo.chunk_elems),
+                        static_cast<cuuint32_t>(geo.box_rows),
+                        static_cast<cuuint32_t>(geo.heads_per_box),
+                        static_cast<cuuint32_t>(geo.num_chunks)};
+  cuuint32_t estride4[4] = {1u, 1u, 1u, 1u};
+  const bool grouped = geo.heads_per_box > 1;
   CUtensorMap map;
   std::memset(&map, 0, sizeof(map));
   CUresult r = g_encode(&map,
                         c->dtype == B200_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        3, const_cast<void*>(base), gdim, gstride, box, estride,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        grouped ? 4 : 3, const_cast<void*>(base), grouped ? gdim4 : gdim,
+                        grouped ? gstride4 : gstride, grouped ? box4 : box,
+                        grouped ? estride4 : estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(B200_ERR_CUDA,
                      "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) +

@@ -36,12 +36,23 @@ struct CacheTmaGeometry {
   int num_chunks;   // head_dim / chunk_elems
   int box_rows;     // tokens per box
   int swizzle_bytes;  // 0, 32, 64 or 128
+  // 1: the 3-D view above, one kv head and one chunk per box.  > 1: the 4-D
+  // head-group view {chunk_elems, token slot, kv head, chunk} (strides row,
+  // head, chunk bytes) whose box {chunk_elems, box_rows, heads_per_box,
+  // num_chunks} lands in shared memory as num_chunks regions of
+  // heads_per_box * box_rows rows, head-major (row = head * box_rows + token).
+  int heads_per_box = 1;
 };
 
 // Chooses the box geometry for a cache and a token tile; returns false with a
 // message if the layout cannot be expressed (see the header's requirements).
 bool cache_tma_geometry(const b200_cache_desc* cache, int tile_tokens, CacheTmaGeometry* geo,
                         std::string* why);
+
+// Head-group geometry: boxes of `heads` kv heads x (64 / heads) tokens, all
+// chunks (one box per tile).  Only for heads in {2, 4} with 64 / heads <=
+// block_size and head_dim 64 or 128; returns false otherwise.
+bool cache_head_group_geometry(const b200_cache_desc* cache, int heads, CacheTmaGeometry* geo);
 
 // Encodes (or returns a cached copy of) the tensor map of one cache tensor.
 int encode_cache_tensor_map(const b200_cache_desc* cache, const void* base,

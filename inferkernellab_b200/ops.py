@@ -88,9 +88,9 @@ class _Workspaces:
             shape_class: tuple = ()) -> torch.Tensor:
         """Workspace of at least ``nbytes``; re-zeroed when ``shape_class`` changes.
 
-        ``shape_class`` = (group, head_dim, dtype): the partial-region size
-        depends on it, so a change could leave old partial bytes under the
-        split counters (see the header's workspace contract).
+        ``shape_class`` = (group, kv heads, head_dim, block size, dtype): the
+        partial-region size depends on it, so a change could leave old partial
+        bytes under the split counters (see the header's workspace contract).
         """
         key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
         with self._lock:
@@ -250,7 +250,8 @@ def paged_decode_attention(query: torch.Tensor, cache, block_tables, context_len
     if need == 0:
         _lib.check(_lib.B200_ERR_INVALID if _lib.last_error() else _lib.B200_ERR_CUDA)
     ws = _WORKSPACES.get(query.device, stream.value or 0, need,
-                         (query.shape[1] // layout.num_kv_heads, layout.head_dim, query.dtype))
+                         (query.shape[1] // layout.num_kv_heads, layout.num_kv_heads,
+                          layout.head_dim, layout.block_size, query.dtype))
     _lib.check(lib.b200_paged_decode(ctypes.byref(desc), ctypes.byref(args), query.data_ptr(),
                                      block_tables.data_ptr(), context_lens.data_ptr(),
                                      out.data_ptr(), ws.data_ptr(), ws.numel(), stream))
@@ -356,7 +357,8 @@ def paged_decode_attention_append(query: torch.Tensor, key: torch.Tensor, value:
     if need == 0:
         _lib.check(_lib.B200_ERR_INVALID if _lib.last_error() else _lib.B200_ERR_CUDA)
     ws = _WORKSPACES.get(device, stream.value or 0, need,
-                         (heads // layout.num_kv_heads, layout.head_dim, dtype))
+                         (heads // layout.num_kv_heads, layout.num_kv_heads, layout.head_dim,
+                          layout.block_size, dtype))
     _lib.check(lib.b200_paged_decode_append(
         ctypes.byref(desc), ctypes.byref(args), ctypes.byref(fused), query.data_ptr(),
         key.data_ptr(), value.data_ptr(), cos.data_ptr() if rope else None,
