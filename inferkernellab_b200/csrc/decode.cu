@@ -847,41 +847,70 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
               merge_w[i] = w;
             }
             named_bar_sync(1, kConsumers);
-            // Pieces in batches of 4: every load of a batch (4 pieces x this
-            // thread's kElems4 outputs) is issued before any is used, so a merge
-            // of n pieces costs about n / 4 L2 round trips.  Pieces with zero
-            // weight (no visible key: their partial is 0/0) are neither loaded
-            // nor added.
-            for (int q0 = 0; q0 < nq; q0 += 4) {
-              float w[4][kElems4];
-              float4 v[4][kElems4];
+            if constexpr (kTrans) {
+              // Pieces in batches of 4 for (at most) 4 outputs of this thread:
+              // every load of a batch (16 float4) is issued before any is used,
+              // so a merge of n pieces costs about n / 4 L2 round trips.  Pieces
+              // with zero weight (no visible key: their partial is 0/0) are
+              // neither loaded nor added.
+              constexpr int kGrp = kElems4 < 4 ? kElems4 : 4;
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const int q = q0 + u;
-                const bool have = q < nq;
-                const long long slot_q = have ? piece_slot(c0 + q) : 0;
+              for (int g0 = 0; g0 < kElems4; g0 += kGrp) {
+                for (int q0 = 0; q0 < nq; q0 += 4) {
+                  float w[4][kGrp];
+                  float4 v[4][kGrp];
 #pragma unroll
-                for (int k4 = 0; k4 < kElems4; ++k4) {
-                  const int e = tid + k4 * kConsumers;
-                  const int row = e / kD4;
-                  const int d4 = e - row * kD4;
-                  const bool in = have && e < GH * kD4;
-                  w[u][k4] = in ? merge_w[q * GH + row] : 0.f;
-                  v[u][k4] = w[u][k4] != 0.f
-                                 ? __ldcg(reinterpret_cast<const float4*>(p.part_o) +
-                                          (slot_q * GH + row) * kD4 + d4)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                  for (int u = 0; u < 4; ++u) {
+                    const int q = q0 + u;
+                    const bool have = q < nq;
+                    const long long slot_q = have ? piece_slot(c0 + q) : 0;
+#pragma unroll
+                    for (int j = 0; j < kGrp; ++j) {
+                      const int e = tid + (g0 + j) * kConsumers;
+                      const int row = e / kD4;
+                      const int d4 = e - row * kD4;
+                      const bool in = have && e < GH * kD4;
+                      w[u][j] = in ? merge_w[q * GH + row] : 0.f;
+                      v[u][j] = w[u][j] != 0.f
+                                    ? __ldcg(reinterpret_cast<const float4*>(p.part_o) +
+                                             (slot_q * GH + row) * kD4 + d4)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                  }
+#pragma unroll
+                  for (int u = 0; u < 4; ++u)
+#pragma unroll
+                    for (int j = 0; j < kGrp; ++j) {
+                      acc[g0 + j].x += w[u][j] * v[u][j].x;
+                      acc[g0 + j].y += w[u][j] * v[u][j].y;
+                      acc[g0 + j].z += w[u][j] * v[u][j].z;
+                      acc[g0 + j].w += w[u][j] * v[u][j].w;
+                    }
                 }
               }
+            } else {
+              // Heads-as-M (G > 16): its main-loop state leaves no registers for
+              // batches; one piece at a time.
 #pragma unroll
-              for (int u = 0; u < 4; ++u)
-#pragma unroll
-                for (int k4 = 0; k4 < kElems4; ++k4) {
-                  acc[k4].x += w[u][k4] * v[u][k4].x;
-                  acc[k4].y += w[u][k4] * v[u][k4].y;
-                  acc[k4].z += w[u][k4] * v[u][k4].z;
-                  acc[k4].w += w[u][k4] * v[u][k4].w;
+              for (int k4 = 0; k4 < kElems4; ++k4) {
+                const int e = tid + k4 * kConsumers;
+                if (e < GH * kD4) {
+                  const int row = e / kD4;
+                  const int d4 = e - row * kD4;
+#pragma unroll 4
+                  for (int q = 0; q < nq; ++q) {
+                    const float w = merge_w[q * GH + row];
+                    if (w == 0.f) continue;
+                    const float4 v = __ldcg(reinterpret_cast<const float4*>(p.part_o) +
+                                            (static_cast<long long>(piece_slot(c0 + q)) * GH +
+                                             row) * kD4 + d4);
+                    acc[k4].x += w * v.x;
+                    acc[k4].y += w * v.y;
+                    acc[k4].z += w * v.z;
+                    acc[k4].w += w * v.w;
+                  }
                 }
+              }
             }
             named_bar_sync(1, kConsumers);
           }
