@@ -36,7 +36,12 @@ import torch
 
 from . import _lib
 from .cache import PagedKVCache
-from .ops import append_kv, paged_decode_attention, paged_prefill_attention_varlen
+from .ops import (
+    append_kv,
+    paged_decode_attention,
+    paged_decode_attention_append,
+    paged_prefill_attention_varlen,
+)
 from .scheduler import InferenceRequest, TokenBudgetScheduler
 
 
@@ -124,6 +129,15 @@ class DecodeCase:
         return kv + qo + table + append
 
     def call(self, cache):
+        # Default: append_kv, then decode (two launches).  --fused-append times
+        # the one-launch form (the append inside the decode kernel): it saves a
+        # launch, but on these small shapes its producer waits for the append
+        # before loading the tile that holds the new token (config-2 sweep mean
+        # 20.1 us fused against 18.8 us unfused, graph-replayed).
+        if self.args.append and getattr(self.args, "fused_append", False):
+            paged_decode_attention_append(self.query, self.new_k, self.new_v, cache, self.tables,
+                                          self.lens, self.slots, out=self.out)
+            return
         if self.args.append:
             append_kv(self.new_k, self.new_v, cache, self.slots)
         paged_decode_attention(self.query, cache, self.tables, self.lens, validate_inputs=False,
@@ -183,6 +197,9 @@ def run(args) -> dict:
             "num_kv_heads": args.num_kv_heads, "head_dim": args.head_dim,
             "block_size": args.block_size, "num_blocks": case.caches[0].layout.num_blocks,
             "block_table_layout": args.layout, "append": bool(args.append),
+            "append_mode": ("none" if not args.append else
+                            "fused into the decode launch" if args.fused_append else
+                            "append_kv + decode (two launches)"),
             "attended_context": case.ctx, "warmup": args.warmup, "iterations": args.iterations,
             "seed": args.seed,
             "timing": "CUDA events with per-sample synchronization; amortised = CUDA graph replay",
@@ -325,6 +342,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--num-blocks", type=int, default=4096)
     p.add_argument("--layout", choices=("interleaved", "shuffled"), default="interleaved")
     p.add_argument("--append", type=int, choices=(0, 1), default=0)
+    p.add_argument("--fused-append", action="store_true",
+                   help="with --append: one launch (append inside the decode kernel)")
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--iterations", type=int, default=30)
     p.add_argument("--rotate", type=int, default=0, help="cache copies (0 = enough to defeat L2)")
