@@ -80,8 +80,8 @@ __host__ __device__ inline TcSmem tc_smem_layout(int num_seqs, int packed) {
   L.q_off = off;
   off += S::kQBytes;
   L.bars_off = off;
-  off += (2 * S::kStages + 10) * 8;  // full, empty, s_full[2], s_free[2], p_full, o_done, q_full,
-                                     // idle, pv_done[2]
+  off += (2 * S::kStages + 9) * 8;  // full, empty, s_full[2], s_free[2], p_full, q_full, idle,
+                                    // pv_done[2]
   L.mask_off = off;
   off += S::kStages * 8;
   L.flags_off = off;
@@ -111,8 +111,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint64_t* s_full = empty_bar + kStages;
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
-  uint64_t* o_done = p_full + 1;
-  uint64_t* q_full = o_done + 1;
+  uint64_t* q_full = p_full + 1;
   uint64_t* mma_idle = q_full + 1;
   uint64_t* pv_done = mma_idle + 1;  // [2]: P V of a tile in S buffer (tile & 1) finished
   uint64_t* stage_mask = reinterpret_cast<uint64_t*>(smem + L.mask_off);
@@ -140,7 +139,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       mbar_init(&s_free[i], kTcSoftmaxWarps * 32);
     }
     mbar_init(p_full, kTcSoftmaxWarps * 32);
-    mbar_init(o_done, 1);
     mbar_init(q_full, kTcSoftmaxWarps * 32);
     mbar_init(mma_idle, 1);
     mbar_init(&pv_done[0], 1);
@@ -260,7 +258,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             tc::mma_f16_tmem_a(tmem + kTcOCol, p_tmem + k * 8,
                                tc::sdesc_sw128(vb + k * 2048, S::kKvRegionBytes, 1024), id_o,
                                np > 0 || k > 0);
-          tc::commit(o_done);
           tc::commit(&pv_done[np & 1]);
           tc::commit(&empty_bar[s]);
           ++np;
@@ -382,13 +379,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       }
       l_sum = l_sum * alpha + ((ps4[0] + ps4[1]) + (ps4[2] + ps4[3]));
 
-      // P V of the previous tile must be done before O is rescaled or P rewritten.
-      if (j > 0) {
-        ok = mbar_wait_bounded(o_done, (j - 1) & 1, abort_flag, p.err, kErrWaitFull);
+      // O is rescaled only when a row of this warp raised its max by more than
+      // 2^8 (rare); only then must P V of the previous tile be complete first.
+      // P_j needs no wait: it goes into the S buffer of tile j - 2, whose P V
+      // finished before S_j could be issued.  The wait uses the per-buffer
+      // pv_done barrier: S_j has been read, so P V of tile j - 2 is done and
+      // pv_done[(j - 1) & 1] has at most one phase outstanding.
+      if (__any_sync(0xffffffffu, rescale)) {
+        ok = mbar_wait_bounded(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.err,
+                               kErrWaitFull);
         if (!ok) break;
         tc::fence_after_sync();
-      }
-      if (__any_sync(0xffffffffu, rescale)) {
         const float a = rescale ? alpha : 1.f;
 #pragma unroll
         for (int cb = 0; cb < D / 32; ++cb) {
@@ -424,8 +425,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       tc::fence_before_sync();
       mbar_arrive(p_full);
     }
+    // The last P V done (it completes after every earlier MMA of the thread).
     if (ok && n_ktiles > 0 &&
-        mbar_wait_bounded(o_done, (n_ktiles - 1) & 1, abort_flag, p.err, kErrWaitFull)) {
+        mbar_wait_bounded(&pv_done[(n_ktiles - 1) & 1], ((n_ktiles - 1) >> 1) & 1, abort_flag,
+                          p.err, kErrWaitFull)) {
       tc::fence_after_sync();
       const float inv = 1.f / l_sum;
       T* orow = nullptr;
