@@ -88,9 +88,15 @@ def test_decode_ragged_long_config3_subset():
     assert_close(out, case.oracle(), torch.bfloat16, "config3 subset")
 
 
-def test_decode_never_reads_unwritten_nan_slots():
-    case = DecodeCase(batch=3, num_heads=8, num_kv_heads=2, head_dim=64, block_size=16,
-                      lens=[7, 16, 45], dtype=torch.float16, nan_fill=True, width=5, seed=5)
+# (Hq, Hkv, D, BS): kv heads per tile 1, 2 (4 heads x 32 tokens needs BS >= 32) and 4.
+HEAD_GROUP_SHAPES = [(8, 2, 64, 16), (8, 2, 64, 32), (32, 8, 128, 16)]
+
+
+@pytest.mark.parametrize("hq,hkv,dim,bs", HEAD_GROUP_SHAPES, ids=["HB1", "HB2", "HB4"])
+def test_decode_never_reads_unwritten_nan_slots(hq, hkv, dim, bs):
+    case = DecodeCase(batch=3, num_heads=hq, num_kv_heads=hkv, head_dim=dim, block_size=bs,
+                      lens=[7, 16, 45], dtype=torch.float16, nan_fill=True,
+                      width=-(-45 // bs) + 1, seed=5)
     out = paged_decode_attention(case.query, case.cache, case.tables, case.lens)
     assert torch.isfinite(out).all()
     assert_close(out, case.oracle(), torch.float16, "nan-poisoned cache")
@@ -117,14 +123,15 @@ def test_decode_rejects_invalid_metadata():
         paged_decode_attention(query.bfloat16(), cache, [[1]], [1])
 
 
-def test_decode_masks_invalid_blocks_without_validation():
+@pytest.mark.parametrize("hq,hkv,dim,bs", HEAD_GROUP_SHAPES, ids=["HB1", "HB2", "HB4"])
+def test_decode_masks_invalid_blocks_without_validation(hq, hkv, dim, bs):
     """validate_inputs=False mirrors the reference kernels: bad pages are skipped."""
-    case = DecodeCase(batch=2, num_heads=8, num_kv_heads=2, head_dim=64, block_size=16,
+    case = DecodeCase(batch=2, num_heads=hq, num_kv_heads=hkv, head_dim=dim, block_size=bs,
                       lens=[40, 40], dtype=torch.float16, seed=9)
     tables = case.tables.clone()
-    tables[1, 1] = case.cache.layout.num_blocks + 5  # tokens 16..31 of request 1 are skipped
+    tables[1, 1] = case.cache.layout.num_blocks + 5  # tokens bs..2bs-1 of request 1 are skipped
     out = paged_decode_attention(case.query, case.cache, tables, case.lens, validate_inputs=False)
-    keep = [list(range(0, 16)) + list(range(32, 40))]
+    keep = [[t for t in range(40) if not bs <= t < 2 * bs]]
     from tests.helpers import to_np
     k = oracle.read_tokens(to_np(case.cache.k), 0, case.tables_list[1], 40)[keep[0]]
     v = oracle.read_tokens(to_np(case.cache.v), 0, case.tables_list[1], 40)[keep[0]]
