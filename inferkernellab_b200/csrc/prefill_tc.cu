@@ -80,8 +80,8 @@ __host__ __device__ inline TcSmem tc_smem_layout(int num_seqs, int packed) {
   L.q_off = off;
   off += S::kQBytes;
   L.bars_off = off;
-  off += (2 * S::kStages + 9) * 8;  // full, empty, s_full[2], s_free[2], p_full, q_full, idle,
-                                    // pv_done[2]
+  off += (2 * S::kStages + 10) * 8;  // full, empty, s_full[2], s_free[2], p_full[2], q_full,
+                                     // idle, pv_done[2]
   L.mask_off = off;
   off += S::kStages * 8;
   L.flags_off = off;
@@ -110,8 +110,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint64_t* empty_bar = full_bar + kStages;
   uint64_t* s_full = empty_bar + kStages;
   uint64_t* s_free = s_full + 2;
+  // [2]: P of the tile in S buffer (tile & 1) written.  One barrier per buffer:
+  // the softmax may write P of tile j + 1 before the MMA thread has taken P of
+  // tile j, but P of tile j + 2 only after P V of tile j (S_{j+2} waits for it),
+  // so each barrier has at most one phase outstanding.
   uint64_t* p_full = s_free + 2;
-  uint64_t* q_full = p_full + 1;
+  uint64_t* q_full = p_full + 2;
   uint64_t* mma_idle = q_full + 1;
   uint64_t* pv_done = mma_idle + 1;  // [2]: P V of a tile in S buffer (tile & 1) finished
   uint64_t* stage_mask = reinterpret_cast<uint64_t*>(smem + L.mask_off);
@@ -138,7 +142,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kTcSoftmaxWarps * 32);
     }
-    mbar_init(p_full, kTcSoftmaxWarps * 32);
+    mbar_init(&p_full[0], kTcSoftmaxWarps * 32);
+    mbar_init(&p_full[1], kTcSoftmaxWarps * 32);
     mbar_init(q_full, kTcSoftmaxWarps * 32);
     mbar_init(mma_idle, 1);
     mbar_init(&pv_done[0], 1);
@@ -248,7 +253,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       unsigned long long last = global_timer_ns();
       while (ok && np < n_ktiles) {
         bool progressed = false;
-        if (np < ns && mbar_test_wait(p_full, np & 1)) {
+        if (np < ns && mbar_test_wait(&p_full[np & 1], (np >> 1) & 1)) {
           tc::fence_after_sync();
           const int s = np % kStages;
           const uint32_t vb = st0 + s * 2 * S::kTileBytes + S::kTileBytes;
@@ -423,7 +428,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       }
       tc::fence_proxy_async_smem();  // zeroed V rows (generic stores) -> the MMA
       tc::fence_before_sync();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1]);
     }
     // The last P V done (it completes after every earlier MMA of the thread).
     if (ok && n_ktiles > 0 &&

@@ -77,6 +77,28 @@ def test_tcgen05_prefill_matches_oracle(cfg, dtype):
     assert check_device_errors() == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_tcgen05_prefill_repeated_calls_are_identical_and_never_time_out(dtype):
+    """The kernel's roles hand tiles over through mbarrier phases; a hand-off that
+    can run two phases ahead of its waiter hangs that CTA until the bounded wait
+    gives up (error bit, garbage rows).  Such races show up only under some
+    timings, so the same multi-tile launch is repeated: every output must equal the
+    first bit for bit (the per-row arithmetic order is fixed) and no wait may
+    time out."""
+    hq, hkv, dim, bs, starts, ends = CASES[0]
+    cache, tables, query = _prefill_case(dtype, hq, hkv, dim, bs, starts, ends, seed=77)
+    check_device_errors()
+    first = paged_prefill_attention(query, cache, tables, starts, ends, kernel="tcgen05")
+    for _ in range(30):
+        out = paged_prefill_attention(query, cache, tables, starts, ends, kernel="tcgen05")
+        assert torch.equal(out, first)
+    torch.cuda.synchronize()
+    assert check_device_errors() == 0
+    want = oracle.paged_prefill_attention(to_np(query), to_np(cache.k), to_np(cache.v),
+                                          KIND[dtype], tables, starts, ends)
+    assert_close(first, want, dtype, "repeated")
+
+
 def test_tcgen05_prefill_packed_nan_poisoned_cache_and_masked_block():
     """Unwritten slots hold NaN; a bad block id in one table is masked (its keys
     are skipped, its V rows never reach O)."""
