@@ -848,19 +848,21 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
             }
             named_bar_sync(1, kConsumers);
             if constexpr (kTrans) {
-              // Pieces in batches of 4 for (at most) 4 outputs of this thread:
-              // every load of a batch (16 float4) is issued before any is used,
-              // so a merge of n pieces costs about n / 4 L2 round trips.  Pieces
+              // Pieces in batches for (at most) 4 outputs of this thread: every
+              // load of a batch (16 float4: 4 pieces x 4 outputs at head_dim 128,
+              // 8 x 2 at 64, 16 x 1 below) is issued before any is used, so a
+              // merge of n pieces costs about n / kPB L2 round trips.  Pieces
               // with zero weight (no visible key: their partial is 0/0) are
               // neither loaded nor added.
               constexpr int kGrp = kElems4 < 4 ? kElems4 : 4;
+              constexpr int kPB = 16 / kGrp;
 #pragma unroll
               for (int g0 = 0; g0 < kElems4; g0 += kGrp) {
-                for (int q0 = 0; q0 < nq; q0 += 4) {
-                  float w[4][kGrp];
-                  float4 v[4][kGrp];
+                for (int q0 = 0; q0 < nq; q0 += kPB) {
+                  float w[kPB][kGrp];
+                  float4 v[kPB][kGrp];
 #pragma unroll
-                  for (int u = 0; u < 4; ++u) {
+                  for (int u = 0; u < kPB; ++u) {
                     const int q = q0 + u;
                     const bool have = q < nq;
                     const long long slot_q = have ? piece_slot(c0 + q) : 0;
@@ -878,7 +880,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
                     }
                   }
 #pragma unroll
-                  for (int u = 0; u < 4; ++u)
+                  for (int u = 0; u < kPB; ++u)
 #pragma unroll
                     for (int j = 0; j < kGrp; ++j) {
                       acc[g0 + j].x += w[u][j] * v[u][j].x;
