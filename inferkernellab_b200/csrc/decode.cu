@@ -781,9 +781,15 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
         if (tid == 0) {
           int last = 0;
           if (!aborted) {
-            __threadfence();  // release this CTA's piece (ordered after the barrier)
-            last = atomicAdd(&p.counters[seg], 1) == npieces - 1;
-            if (last) __threadfence();  // acquire the other pieces
+            // One acquire-release RMW: it releases this CTA's piece (the barrier
+            // above ordered every consumer's partial writes before it) and, for
+            // the last piece, acquires the other pieces for the merge below.
+            int prev;
+            asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;"
+                         : "=r"(prev)
+                         : "l"(&p.counters[seg])
+                         : "memory");
+            last = prev == npieces - 1;
           }
           *merge_flag = last;
         }
