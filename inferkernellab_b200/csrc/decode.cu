@@ -435,12 +435,11 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   const int GH = G * HB;            // query heads per segment
 
   // ---- prologue: effective lengths and the tile prefix over requests ----
-  const long long cap = static_cast<long long>(p.table_width) * p.block_size;
-  for (int i = tid; i < B; i += kDecThreads) {
-    long long len = load_index(p.lens, i, p.lens64);
-    len = len < 0 ? 0 : (len > cap ? cap : len);
-    len_s[i] = static_cast<int>(len);
-  }
+  // Launched with programmatic stream serialization, this grid may start while
+  // the previous kernel on the stream is finishing: only barrier set-up and the
+  // tensor-map prefetch (kernel parameters) run before griddepcontrol.wait,
+  // which returns once that kernel has completed and its writes are visible.
+  // Every global access comes after it.
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -452,6 +451,16 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   if (warp == kDecConsumerWarps && lane == 0) {
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The next kernel on the stream may be scheduled now; its CTAs run their own
+  // set-up on SMs this grid leaves and then wait for it to complete.
+  if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const long long cap = static_cast<long long>(p.table_width) * p.block_size;
+  for (int i = tid; i < B; i += kDecThreads) {
+    long long len = load_index(p.lens, i, p.lens64);
+    len = len < 0 ? 0 : (len > cap ? cap : len);
+    len_s[i] = static_cast<int>(len);
   }
   __syncthreads();
   {
@@ -998,7 +1007,21 @@ static int launch_decode_t(const CUtensorMap& kmap, const CUtensorMap& vmap,
   if (err != cudaSuccess) return cuda_status(err, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
   *grid_out = num_sms * (per_sm_max > per_sm ? per_sm_max : per_sm);
   if (dry_run) return B200_OK;
-  kern<<<grid, kDecThreads, smem, stream>>>(kmap, vmap, p);
+  // Programmatic stream serialization: the grid may be scheduled while the
+  // previous kernel on the stream finishes (the kernel waits for it before any
+  // global access), hiding the launch and set-up behind that kernel's tail.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t lerr = cudaLaunchKernelEx(&cfg, kern, kmap, vmap, p);
+  if (lerr != cudaSuccess) return cuda_status(lerr, "paged_decode_kernel launch");
   return cuda_status(cudaGetLastError(), "paged_decode_kernel launch");
 }
 
