@@ -151,6 +151,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     *abort_flag = 0;
     fence_mbar_init();
   }
+  // Launched with programmatic stream serialization: the CTA may start while
+  // the previous kernel on the stream (typically the KV append of the same
+  // batch) finishes.  Nothing above touches global memory; griddepcontrol.wait
+  // returns once that kernel has completed and its writes are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // ---- which (sequence, 128-row query tile) this CTA owns ----
   int b = 0, qt = 0;
@@ -485,7 +491,18 @@ int launch_tc_t(const CUtensorMap& kmap, const CUtensorMap& vmap, const PrefillP
     if (err != cudaSuccess) return cuda_status(err, "cudaFuncSetAttribute(prefill tcgen05 smem)");
     configured[dev] = smem;
   }
-  kern<<<grid, kTcThreads, smem, stream>>>(kmap, vmap, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t lerr = cudaLaunchKernelEx(&cfg, kern, kmap, vmap, p);
+  if (lerr != cudaSuccess) return cuda_status(lerr, "paged_prefill_tc_kernel launch");
   return cuda_status(cudaGetLastError(), "paged_prefill_tc_kernel launch");
 }
 
