@@ -506,7 +506,22 @@ def run_reference(args, world, rank) -> dict | None:
     }
 
 
+def _json_stdout():
+    """Keep stdout for this program's JSON line alone.
+
+    Libraries may print to stdout (NCCL prints a version banner when the
+    environment sets NCCL_DEBUG=VERSION, as the GPU boxes here do): file
+    descriptor 1 is pointed at stderr for the rest of the run, and the JSON line
+    goes to a duplicate of the original stdout.
+    """
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
 def main(argv=None) -> int:
+    json_out = _json_stdout()
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=2000)
@@ -525,7 +540,7 @@ def main(argv=None) -> int:
     if args.impl == "reference":
         record = run_reference(args, world, rank)
         if record:
-            print(json.dumps(record), flush=True)
+            print(json.dumps(record), file=json_out, flush=True)
         return 0
     if world > 1:
         import datetime
@@ -536,7 +551,7 @@ def main(argv=None) -> int:
     try:
         record = run_ours(args, world, rank, local)
         if record:
-            print(json.dumps(record), flush=True)
+            print(json.dumps(record), file=json_out, flush=True)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()
