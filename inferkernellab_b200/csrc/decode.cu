@@ -106,7 +106,7 @@ struct DecodeSmem {
   int stage_bytes;  // K + V of one stage
   int bars_off;     // full[S], empty[S]
   int mask_off;     // uint64 per stage
-  int flags_off;    // abort, merge flag
+  int flags_off;    // abort, merge flag, most tiles of one segment
   int red_m_off, red_l_off, red_w_off, row_off, red_o_off, merge_w_off;
   int table_off;    // producer's block-table window
   int len_off, begin_off, scan_off;
@@ -380,6 +380,9 @@ __device__ __forceinline__ void store4(typename E::T* dst, float4 v) {
 }
 
 constexpr int kMinTilesPerCta = 2;  // fewer split pieces on small problems
+// Heads-as-M variants (G > 16): a segment of at most this many tiles is not
+// split when the grid has a CTA for every segment (see the range choice).
+constexpr int kSegWholeMaxTiles = 10;
 
 // FUSED: the new-token append (and rotary embedding) of b200_paged_decode_append
 // is compiled in; the plain decode instantiation carries none of that code.
@@ -412,6 +415,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   uint64_t* stage_mask = reinterpret_cast<uint64_t*>(smem + L.mask_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.flags_off);
   int* merge_flag = reinterpret_cast<int*>(smem + L.flags_off + 4);
+  int* max_seg_tiles = reinterpret_cast<int*>(smem + L.flags_off + 8);
   float* red_m = reinterpret_cast<float*>(smem + L.red_m_off);
   float* red_l = reinterpret_cast<float*>(smem + L.red_l_off);
   float* red_w = reinterpret_cast<float*>(smem + L.red_w_off);
@@ -446,6 +450,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       mbar_init(&empty_bar[s], kDecConsumerWarps);
     }
     *abort_flag = 0;
+    *max_seg_tiles = 0;
     fence_mbar_init();
   }
   if (warp == kDecConsumerWarps && lane == 0) {
@@ -476,6 +481,11 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       acc += ((len_s[i] + TT - 1) / TT) * HG;
     }
     if (tid == 0) begin_s[B] = total_all;
+    if constexpr (MT > 0) {
+      int most = 0;
+      for (int i = lo; i < hi; ++i) most = max(most, (len_s[i] + TT - 1) / TT);
+      if (most > 0) atomicMax(max_seg_tiles, most);
+    }
   }
   __syncthreads();
 
@@ -495,13 +505,30 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   }
 
   // ---- this CTA's contiguous range of tiles (stream-K) ----
+  // In the heads-as-M variants a split piece (publish + merge of the pieces)
+  // costs ~8 us against ~1 us per tile on small batches, so when every segment
+  // is short and the grid has a CTA for each, CTA b takes segment b whole and
+  // nothing is split.  Otherwise the tiles are cut into equal ranges.
   const int total = begin_s[B];
-  const int ctas = min(static_cast<int>(gridDim.x),
-                       max(1, (total + kMinTilesPerCta - 1) / kMinTilesPerCta));
+  const bool whole_segs = MT > 0 && B * HG <= static_cast<int>(gridDim.x) &&
+                          *max_seg_tiles <= kSegWholeMaxTiles;
+  const int ctas = whole_segs ? B * HG
+                              : min(static_cast<int>(gridDim.x),
+                                    max(1, (total + kMinTilesPerCta - 1) / kMinTilesPerCta));
   if (static_cast<int>(blockIdx.x) >= ctas) return;
-  const int per_cta = (total + ctas - 1) / ctas;
-  const int my_begin = min(total, static_cast<int>(blockIdx.x) * per_cta);
-  const int my_end = min(total, my_begin + per_cta);
+  int per_cta, my_begin, my_end;
+  if (whole_segs) {
+    const int r = static_cast<int>(blockIdx.x) / HG;
+    const int h = static_cast<int>(blockIdx.x) - r * HG;
+    const int nt = (len_s[r] + TT - 1) / TT;
+    my_begin = begin_s[r] + h * nt;
+    my_end = my_begin + nt;
+    per_cta = max(1, nt);  // every segment is complete: no piece slots are used
+  } else {
+    per_cta = (total + ctas - 1) / ctas;
+    my_begin = min(total, static_cast<int>(blockIdx.x) * per_cta);
+    my_end = min(total, my_begin + per_cta);
+  }
   const int n_tiles = my_end - my_begin;
   if (n_tiles <= 0) return;
   // Fused append: the consumers write the new tokens (and stage the rotated q)

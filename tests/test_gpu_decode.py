@@ -46,6 +46,8 @@ SHAPES = [
     (3, 8, 8, 128, 16, [1, 63, 64]),                     # MHA, tile edges
     (5, 32, 1, 64, 16, [5, 129, 300, 16, 17]),           # MQA G=32
     (2, 64, 1, 64, 16, [100, 257]),                      # G=64
+    (3, 32, 1, 64, 16, [640, 1, 65]),                    # G=32, 10 tiles: one CTA per segment
+    (3, 32, 1, 64, 16, [641, 1, 65]),                    # G=32, 11 tiles: split ranges
     (3, 16, 2, 128, 16, [1000, 3, 65]),                  # G=8, D128
     (4, 24, 2, 32, 8, [40, 1, 77, 128]),                 # G=12 (padded M tile), D32
     (2, 4, 2, 16, 8, [19, 23]),                          # the reference Triton test shape

@@ -57,6 +57,7 @@ SHAPES = [
     (3, 24, 2, 32, 8, [40, 1, 77]),                    # G = 12 (N = 16 variant)
     (2, 64, 2, 64, 16, [100, 257]),                    # G = 32 (heads as M)
     (2, 64, 1, 128, 16, [300, 31]),                    # G = 64
+    (3, 32, 1, 64, 16, [641, 9, 700]),                 # G = 32, split ranges (> 10 tiles)
     (2, 4, 2, 16, 8, [19, 23]),                        # D = 16
     (2, 8, 2, 64, 128, [130, 600]),                    # block size 128
 ]
