@@ -380,9 +380,15 @@ __device__ __forceinline__ void store4(typename E::T* dst, float4 v) {
 }
 
 constexpr int kMinTilesPerCta = 2;  // fewer split pieces on small problems
-// Heads-as-M variants (G > 16): a segment of at most this many tiles is not
-// split when the grid has a CTA for every segment (see the range choice).
+// A segment of at most this many tiles is not split when the grid has a CTA
+// for every segment (see the range choice).
 constexpr int kSegWholeMaxTiles = 10;
+
+// A CTA for every segment, and few enough tiles that no segment can be longer
+// than the limit on average (config-3-sized batches skip the length pass).
+__device__ __forceinline__ bool decode_whole_segs_possible(int segments, int tiles, int grid) {
+  return segments <= grid && tiles <= segments * kSegWholeMaxTiles;
+}
 
 // FUSED: the new-token append (and rotary embedding) of b200_paged_decode_append
 // is compiled in; the plain decode instantiation carries none of that code.
@@ -481,7 +487,8 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       acc += ((len_s[i] + TT - 1) / TT) * HG;
     }
     if (tid == 0) begin_s[B] = total_all;
-    if constexpr (MT > 0) {
+    // The longest segment, only where whole segments are possible at all.
+    if (decode_whole_segs_possible(B * HG, total_all, static_cast<int>(gridDim.x))) {
       int most = 0;
       for (int i = lo; i < hi; ++i) most = max(most, (len_s[i] + TT - 1) / TT);
       if (most > 0) atomicMax(max_seg_tiles, most);
@@ -505,12 +512,13 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   }
 
   // ---- this CTA's contiguous range of tiles (stream-K) ----
-  // In the heads-as-M variants a split piece (publish + merge of the pieces)
-  // costs ~8 us against ~1 us per tile on small batches, so when every segment
-  // is short and the grid has a CTA for each, CTA b takes segment b whole and
-  // nothing is split.  Otherwise the tiles are cut into equal ranges.
+  // On small batches a split piece (publish + merge of the pieces) costs
+  // several us against ~1 us per tile (~8 us in the heads-as-M variants), so
+  // when every segment is short and the grid has a CTA for each, CTA b takes
+  // segment b whole and nothing is split.  Otherwise the tiles are cut into
+  // equal ranges.
   const int total = begin_s[B];
-  const bool whole_segs = MT > 0 && B * HG <= static_cast<int>(gridDim.x) &&
+  const bool whole_segs = decode_whole_segs_possible(B * HG, total, static_cast<int>(gridDim.x)) &&
                           *max_seg_tiles <= kSegWholeMaxTiles;
   const int ctas = whole_segs ? B * HG
                               : min(static_cast<int>(gridDim.x),
