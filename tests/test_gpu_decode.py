@@ -69,6 +69,20 @@ def test_decode_matches_oracle(shape, dtype):
     assert_close(out, case.oracle(), dtype, str(shape))
 
 
+@pytest.mark.parametrize("batch", [150, 400], ids=["whole_segments", "split_ranges"])
+def test_decode_many_short_segments(batch):
+    """Short requests (at most 10 tiles of 32 tokens each at Hkv 2, D 64): with a CTA
+    per segment every request runs unsplit, CTA b on request b; with more segments
+    than CTAs the kernel falls back to equal split ranges.  Both must match."""
+    rng = np.random.default_rng(batch)
+    lens = rng.integers(1, 321, size=batch).tolist()
+    case = DecodeCase(batch=batch, num_heads=8, num_kv_heads=2, head_dim=64, block_size=16,
+                      lens=lens, dtype=torch.bfloat16, seed=batch)
+    out = paged_decode_attention(case.query, case.cache, case.tables, case.lens)
+    assert_close(out, case.oracle(), torch.bfloat16, f"batch {batch}")
+    assert check_device_errors() == 0
+
+
 @pytest.mark.parametrize("table_dtype", [torch.int32, torch.int64])
 def test_decode_int64_metadata_layer_and_scale(table_dtype):
     case = DecodeCase(batch=3, num_heads=16, num_kv_heads=4, head_dim=64, block_size=16,
