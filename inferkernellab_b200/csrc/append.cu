@@ -34,6 +34,10 @@ struct AppendParams {
 
 template <typename V>
 __global__ void __launch_bounds__(256) append_kv_kernel(const AppendParams p) {
+  // Launched with programmatic stream serialization: no global access before
+  // the previous kernel on the stream has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int vec_per_row = p.row_bytes / static_cast<int>(sizeof(V));
   const long long per_token = static_cast<long long>(p.num_kv_heads) * vec_per_row;
   const long long total = p.num_tokens * per_token;
@@ -104,11 +108,12 @@ int launch_append_kv(const b200_cache_desc* c, int32_t layer, const void* key, c
   const int threads = 256;
   long long blocks = (total + threads - 1) / threads;
   if (blocks > 148LL * 64) blocks = 148LL * 64;
-  if (vec16)
-    append_kv_kernel<uint4><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p);
-  else
-    append_kv_kernel<uint16_t><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p);
-  return cuda_status(cudaGetLastError(), "append_kv_kernel launch");
+  const cudaError_t err =
+      vec16 ? launch_dependent(append_kv_kernel<uint4>, dim3(static_cast<unsigned>(blocks)),
+                               dim3(threads), 0, stream, p)
+            : launch_dependent(append_kv_kernel<uint16_t>, dim3(static_cast<unsigned>(blocks)),
+                               dim3(threads), 0, stream, p);
+  return cuda_status(err, "append_kv_kernel launch");
 }
 
 }  // namespace b200

@@ -32,6 +32,10 @@ struct SlotParams {
 __global__ void __launch_bounds__(kMetaThreads) build_slot_mapping_kernel(const SlotParams p) {
   extern __shared__ long long prefix_s[];  // [num_seqs + 1]
   __shared__ long long scan_s[kMetaThreads];
+  // Launched with programmatic stream serialization: no global access before
+  // the previous kernel on the stream has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int tid = threadIdx.x;
   const int B = p.num_seqs;
   const int chunk = (B + kMetaThreads - 1) / kMetaThreads;
@@ -126,8 +130,9 @@ int launch_build_slot_mapping(const void* block_tables, int32_t table_dtype, int
                                            static_cast<int>(smem));
     if (err != cudaSuccess) return cuda_status(err, "cudaFuncSetAttribute(slot mapping smem)");
   }
-  build_slot_mapping_kernel<<<static_cast<unsigned>(blocks), kMetaThreads, smem, stream>>>(p);
-  return cuda_status(cudaGetLastError(), "build_slot_mapping_kernel launch");
+  return cuda_status(launch_dependent(build_slot_mapping_kernel, dim3(static_cast<unsigned>(blocks)),
+                                      dim3(kMetaThreads), smem, stream, p),
+                     "build_slot_mapping_kernel launch");
 }
 
 struct ValidateParams {
