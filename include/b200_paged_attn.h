@@ -132,11 +132,18 @@ B200_API int b200_paged_decode(const b200_cache_desc* cache, const b200_decode_a
  *    at head_dim 128); use b200_paged_decode with a workspace for those.
  *  - The first call on a device, with that device current, resolves the
  *    array's device address (cudaGetSymbolAddress); make that first call
- *    before any stream capture.
+ *    before any stream capture.  The address is kept per device and per
+ *    current context, so a new context on that device (after cudaDeviceReset)
+ *    resolves it again.
  *  - All calls share the one array and it keeps the last call's contents:
  *    each call zeroes the error word and split counters (two cudaMemsetAsync
  *    on `stream`) before its launch.  Calls whose executions overlap on the
  *    GPU (different streams without ordering) race on the array.
+ *  - Device-side conditions of a call (a masked out-of-pool block id, a
+ *    bounded wait that gave up: the B200_DEVERR_* bits) land in the array's
+ *    error word; read it after the call, before the next one clears it, with
+ *    b200_read_error_word on the address from
+ *    b200_paged_decode_noalloc_error_word.
  */
 B200_API int b200_paged_decode_noalloc(const b200_cache_desc* cache, const b200_decode_args* args,
                                        const void* query, const void* block_tables,
@@ -144,6 +151,13 @@ B200_API int b200_paged_decode_noalloc(const b200_cache_desc* cache, const b200_
 
 /* Size in bytes of the static scratch array used by b200_paged_decode_noalloc. */
 B200_API size_t b200_paged_decode_noalloc_scratch_bytes(void);
+
+/* Device address of the error word inside that static array, for the current
+ * device (no counterpart in the reference).  Resolves the array's address like
+ * the first b200_paged_decode_noalloc call does, and allocates nothing.  Pass
+ * the address to b200_read_error_word after a b200_paged_decode_noalloc call
+ * on the same device. */
+B200_API int b200_paged_decode_noalloc_error_word(uint32_t** error_word_out);
 
 /* ------------------------------------------------------------------ append
  * Reshape-and-cache: cache[layer, slot/BS, slot%BS, h, :] = key[t, h, :] (and V)
@@ -226,6 +240,18 @@ B200_API int b200_rope_append_kv(const b200_cache_desc* cache, const b200_rope_a
  * No counterpart in the reference. */
 B200_API int b200_tc_selftest(const void* a, const void* b, const void* v, float* c1, float* c2,
                               float* c3, int32_t dtype, uint32_t* error_word, void* stream);
+
+/* b200_wait_selftest: runs the bounded mbarrier wait that every kernel of this
+ * library uses (1 s limit there) with limit_ns instead, in a one-CTA kernel.
+ * With arrive = 0 nobody arrives: the first waiter gives up after limit_ns,
+ * sets B200_DEVERR_WAIT_FULL in *error_word and raises the CTA abort flag,
+ * through which the other waiters leave; the kernel returns and the context
+ * stays usable.  With arrive = 1 every wait completes and nothing is set.
+ * result (device uint32[3]): waits completed in the first / second waiting
+ * warp, and the ns the first waiter spent.  limit_ns in [1000, 2e9].
+ * No counterpart in the reference. */
+B200_API int b200_wait_selftest(int64_t limit_ns, int32_t arrive, uint32_t* result,
+                                uint32_t* error_word, void* stream);
 
 /* ------------------------------------------------- decoder-layer helpers
  * Kernels for the Llama layer around the attention call (the reference's

@@ -39,12 +39,14 @@ EXPORTED_SYMBOLS = (
     "b200_paged_decode",
     "b200_paged_decode_noalloc",
     "b200_paged_decode_noalloc_scratch_bytes",
+    "b200_paged_decode_noalloc_error_word",
     "b200_append_kv",
     "b200_rope_append_kv",
     "b200_paged_decode_append",
     "b200_add_rmsnorm",
     "b200_silu_mul",
     "b200_tc_selftest",
+    "b200_wait_selftest",
     "b200_paged_prefill",
     "b200_build_slot_mapping",
     "b200_validate_decode_metadata",
@@ -151,6 +153,7 @@ _PROTOTYPES = {
                                                  ctypes.POINTER(DecodeArgs), _vp, _vp, _vp, _vp,
                                                  _vp]),
     "b200_paged_decode_noalloc_scratch_bytes": (ctypes.c_size_t, []),
+    "b200_paged_decode_noalloc_error_word": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p)]),
     "b200_append_kv": (ctypes.c_int, [ctypes.POINTER(CacheDesc), _i32, _vp, _vp, _i64, _i64, _i64,
                                       _i64, _i64, _vp, _i32, _vp, _vp]),
     "b200_paged_decode_append": (ctypes.c_int, [ctypes.POINTER(CacheDesc),
@@ -164,6 +167,7 @@ _PROTOTYPES = {
     "b200_add_rmsnorm": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                         _i64, ctypes.c_float, _i32, _vp]),
     "b200_silu_mul": (ctypes.c_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
+    "b200_wait_selftest": (ctypes.c_int, [_i64, _i32, _vp, _vp, _vp]),
     "b200_tc_selftest": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp]),
     "b200_paged_prefill": (ctypes.c_int, [ctypes.POINTER(CacheDesc), ctypes.POINTER(PrefillArgs),
                                           _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),

@@ -234,17 +234,18 @@ def sweep_config2(args):
                     yield run(ns)
 
 
-def run_prefill(args) -> dict:
-    """BASELINE config 4: 24 prompts U[17,512], token budget 2048, packed prefill + append."""
-    device = _cuda_device(args.device)
-    torch.cuda.set_device(device)
-    dtype = torch.bfloat16
-    hq, hkv, dim, bs = 32, 8, 128, 16
-    gen = torch.Generator().manual_seed(args.seed)
-    lens = torch.randint(args.prefill_min_len, args.prefill_max_len + 1, (args.prefill_prompts,),
-                         generator=gen).tolist()
-    sched = TokenBudgetScheduler(max_num_seqs=max(32, args.prefill_prompts),
-                                 max_num_batched_tokens=2048)
+def config4_plan(seed: int, prompts: int = 24, min_len: int = 17, max_len: int = 512,
+                 budget: int = 2048, block_size: int = 16):
+    """BASELINE config 4's batches: seeded prompt lengths packed under the token budget.
+
+    Returns ``(lens, batches, tables, num_blocks)``: ``batches`` lists, per
+    budget batch the ``TokenBudgetScheduler`` forms (FCFS, only the head request
+    chunked), ``(request, start, end)`` of each scheduled range; ``tables`` are
+    the requests' block-table rows over a shuffled pool of ``num_blocks``.
+    """
+    gen = torch.Generator().manual_seed(seed)
+    lens = torch.randint(min_len, max_len + 1, (prompts,), generator=gen).tolist()
+    sched = TokenBudgetScheduler(max_num_seqs=max(32, prompts), max_num_batched_tokens=budget)
     reqs = [InferenceRequest(i, n, 1) for i, n in enumerate(lens)]
     for r in reqs:
         sched.add(r)
@@ -255,15 +256,26 @@ def run_prefill(args) -> dict:
         if b.phase != "prefill":
             break
         batches.append([(r.request_id, before[r.request_id], r.cached_tokens) for r in b.requests])
-    need = [-(-n // bs) for n in lens]
+    need = [-(-n // block_size) for n in lens]
     num_blocks = sum(need) + 8
-    cache = PagedKVCache(num_blocks, bs, hkv, dim, dtype=dtype, device=device)
     perm = torch.randperm(num_blocks, generator=gen).tolist()
     width = max(need)
     tables, cur = [], 0
     for n in need:
         tables.append(perm[cur:cur + n] + [0] * (width - n))
         cur += n
+    return lens, batches, tables, num_blocks
+
+
+def run_prefill(args) -> dict:
+    """BASELINE config 4: 24 prompts U[17,512], token budget 2048, packed prefill + append."""
+    device = _cuda_device(args.device)
+    torch.cuda.set_device(device)
+    dtype = torch.bfloat16
+    hq, hkv, dim, bs = 32, 8, 128, 16
+    lens, batches, tables, num_blocks = config4_plan(
+        args.seed, args.prefill_prompts, args.prefill_min_len, args.prefill_max_len)
+    cache = PagedKVCache(num_blocks, bs, hkv, dim, dtype=dtype, device=device)
     tables = torch.tensor(tables, dtype=torch.int32, device=device)
     work = []
     flops = 0.0
@@ -329,6 +341,104 @@ def run_prefill(args) -> dict:
     }
 
 
+def _reference_modules():
+    """The reference project installed under ``baseline/_ref`` (repository root)."""
+    path = Path(__file__).resolve().parent.parent / "baseline" / "_ref"
+    if not (path / "inferkernellab").is_dir():
+        raise RuntimeError("the reference is not installed under baseline/_ref")
+    if str(path) not in sys.path:
+        sys.path.insert(0, str(path))
+    from inferkernellab import attention, cache, triton_ops  # the reference's own modules
+
+    return attention, cache, triton_ops
+
+
+def run_reference_gpu(args) -> list[dict]:
+    """The reference's own GPU decode backends beside this library's kernel.
+
+    Configs 1 and 3 on the same B200, the same inputs in one cache object (the
+    reference's ``PagedKVCache``, which this library's ops also accept):
+    ``triton_paged`` (reference ``triton_ops.py:404-478``),
+    ``triton_paged_grouped`` (``:481-610``), ``paged_sdpa``
+    (``attention.py:178-227``) and ``b200_paged``.  Each backend is timed two
+    ways with CUDA events: one call at a time with a synchronisation between
+    calls (median), and ``--iterations`` calls back to back (mean).  Inputs
+    validation is off where a backend has the switch.  The outputs are checked
+    against this library's before timing.
+    """
+    from .workloads import workload_tensors
+
+    ref_attention, ref_cache, ref_triton = _reference_modules()
+    device = _cuda_device(args.device)
+    torch.cuda.set_device(device)
+    cases = []
+    # config 1: B4, ctx 512, Hq32/Hkv8, D64, BS16, 159 blocks, fp16, seeded shuffled tables
+    gen = torch.Generator().manual_seed(args.seed)
+    c1 = ref_cache.PagedKVCache(159, 16, 8, 64, dtype=torch.float16, device=device)
+    c1.k.copy_(torch.randn(c1.k.shape, generator=gen).half())
+    c1.v.copy_(torch.randn(c1.v.shape, generator=gen).half())
+    perm = torch.randperm(159, generator=gen)
+    tables1 = perm[:4 * 32].view(4, 32).to(torch.int32).to(device)
+    lens1 = torch.full((4,), 512, dtype=torch.int32, device=device)
+    q1 = torch.randn(4, 32, 64, generator=gen).half().to(device)
+    cases.append(("config1", c1, q1, tables1, lens1, [512] * 4, 16))
+    # config 3: the bench's seed-0 batch
+    t = workload_tensors(args.seed, device)
+    c3 = ref_cache.PagedKVCache(t["num_blocks"], 16, 8, 128, dtype=torch.bfloat16, device=device)
+    c3.k, c3.v = t["k"], t["v"]
+    cases.append(("config3", c3, t["query"], t["tables"].to(device),
+                  torch.tensor(t["lens"], dtype=torch.int32, device=device), t["lens"], 16))
+    records = []
+    for name, cache, q, tables, lens, lens_list, bs in cases:
+        lay = cache.layout
+        es = q.element_size()
+        nbytes = (sum(lens_list) * lay.num_kv_heads * lay.head_dim * es * 2
+                  + 2 * q.numel() * es + sum(-(-n // bs) for n in lens_list) * 4 + 4 * len(lens_list))
+        backends = {
+            "b200_paged": lambda: paged_decode_attention(q, cache, tables, lens,
+                                                         validate_inputs=False),
+            "triton_paged": lambda: ref_triton.paged_decode_attention_triton(
+                q, cache, tables, lens, validate_inputs=False),
+            "triton_paged_grouped": lambda: ref_triton.paged_decode_attention_triton_grouped(
+                q, cache, tables, lens, validate_inputs=False),
+            "paged_sdpa": lambda: ref_attention.paged_decode_attention_sdpa(q, cache, tables, lens),
+        }
+        want = backends["b200_paged"]().float()
+        for backend, fn in backends.items():
+            diff = float((fn().float() - want).abs().max())
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize(device)
+            single = []
+            for _ in range(args.iterations):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                e1.synchronize()
+                single.append(e0.elapsed_time(e1))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.iterations):
+                fn()
+            e1.record()
+            e1.synchronize()
+            b2b = e0.elapsed_time(e1) / args.iterations
+            p50 = statistics.median(single)
+            records.append({
+                "benchmark": "reference_gpu_decode", "config": name, "backend": backend,
+                "per_call_p50_ms": round(p50, 5), "back_to_back_ms": round(b2b, 5),
+                "algorithmic_bytes": nbytes,
+                "per_call_gbs": round(nbytes / (p50 * 1e-3) / 1e9, 1),
+                "back_to_back_gbs": round(nbytes / (b2b * 1e-3) / 1e9, 1),
+                "max_abs_diff_vs_b200_paged": diff,
+                "l2_note": "working set fits in the 126 MB L2" if nbytes < 64e6 else
+                           "working set exceeds L2",
+                "device": torch.cuda.get_device_name(device),
+            })
+    return records
+
+
 def build_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description="B200 paged decode attention microbenchmark")
     p.add_argument("--device", default="cuda")
@@ -358,6 +468,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--prefill-max-len", type=int, default=512)
     p.add_argument("--profile-kernel", action="store_true",
                    help="one decode launch between cudaProfilerStart/Stop (ncu --profile-from-start off)")
+    p.add_argument("--reference-gpu", action="store_true",
+                   help="time the reference's own GPU decode backends (baseline/_ref) beside "
+                        "b200_paged on configs 1 and 3")
     p.add_argument("--output", type=Path)
     return p
 
@@ -376,7 +489,9 @@ def main(argv=None) -> None:
         print(json.dumps({"profile_mode": "single b200 paged-decode launch"}))
         return
     records = []
-    if args.prefill:
+    if args.reference_gpu:
+        records.extend(run_reference_gpu(args))
+    elif args.prefill:
         records.append(run_prefill(args))
     elif args.sweep == "config2":
         records.extend(sweep_config2(args))

@@ -19,6 +19,8 @@ namespace b200 {
 const char* last_error_cstr();
 int launch_tc_selftest(const void* a, const void* b, const void* v, float* c1, float* c2,
                        float* c3, int32_t dtype, uint32_t* err, cudaStream_t stream);
+int launch_wait_selftest(int64_t limit_ns, int32_t arrive, uint32_t* result, uint32_t* err,
+                         cudaStream_t stream);
 }
 
 namespace {
@@ -70,6 +72,10 @@ size_t b200_paged_decode_noalloc_scratch_bytes(void) {
   return b200::decode_noalloc_scratch_bytes();
 }
 
+int b200_paged_decode_noalloc_error_word(uint32_t** error_word_out) {
+  return guarded([&] { return b200::decode_noalloc_error_word(error_word_out); });
+}
+
 int b200_append_kv(const b200_cache_desc* cache, int32_t layer, const void* key, const void* value,
                    int64_t num_tokens, int64_t key_stride_token, int64_t key_stride_head,
                    int64_t value_stride_token, int64_t value_stride_head, const void* slots,
@@ -107,6 +113,13 @@ int b200_tc_selftest(const void* a, const void* b, const void* v, float* c1, flo
                      float* c3, int32_t dtype, uint32_t* error_word, void* stream) {
   return guarded([&] {
     return b200::launch_tc_selftest(a, b, v, c1, c2, c3, dtype, error_word, as_stream(stream));
+  });
+}
+
+int b200_wait_selftest(int64_t limit_ns, int32_t arrive, uint32_t* result, uint32_t* error_word,
+                       void* stream) {
+  return guarded([&] {
+    return b200::launch_wait_selftest(limit_ns, arrive, result, error_word, as_stream(stream));
   });
 }
 

@@ -96,15 +96,18 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// `limit_ns` is kWaitLimitNs everywhere except the wait self-test, which gives
+// it a short limit to drive the give-up path.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag,
-                                                  uint32_t* err_word, uint32_t err_code) {
+                                                  uint32_t* err_word, uint32_t err_code,
+                                                  unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       if (err_word) atomicOr(err_word, err_code);
       return false;

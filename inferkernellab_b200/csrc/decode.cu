@@ -1321,28 +1321,64 @@ static __device__ __align__(256) uint8_t g_decode_noalloc_scratch[kDecodeNoAlloc
 
 namespace {
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {};  // device address of the array, per device
+// Device address of the array per device index, with the context it was
+// resolved in: a different current context on that device (after
+// cudaDeviceReset, or a context the caller made with the driver API) resolves
+// it again instead of reusing a stale address.
+struct NoAllocAddress {
+  CUcontext ctx = nullptr;
+  void* ptr = nullptr;
+};
+NoAllocAddress g_noalloc_addr[64];
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
 }  // namespace
 
 // Host code may not use the array's name as a device address; resolve it once
-// per device, with that device current.
+// per device (and context), with that device current.
 static int noalloc_scratch_address(void** out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return cuda_status(err, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return set_error(B200_ERR_UNSUPPORTED, "device index >= 64");
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_ctx_get_current == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q);
+    if (err != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return set_error(B200_ERR_CUDA, "cuCtxGetCurrent entry point unavailable");
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+  }
+  // cudaGetDevice does not create the primary context; a runtime call that
+  // needs one does, so resolve the symbol first when nothing is current yet.
+  CUcontext ctx = nullptr;
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+  NoAllocAddress& slot = g_noalloc_addr[dev];
+  if (slot.ptr == nullptr || ctx == nullptr || slot.ctx != ctx) {
     void* ptr = nullptr;
     err = cudaGetSymbolAddress(&ptr, g_decode_noalloc_scratch);
     if (err != cudaSuccess) return cuda_status(err, "cudaGetSymbolAddress(decode scratch)");
-    g_noalloc_ptr[dev] = ptr;
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    slot.ctx = ctx;
+    slot.ptr = ptr;
   }
-  *out = g_noalloc_ptr[dev];
+  *out = slot.ptr;
   return B200_OK;
 }
 
 size_t decode_noalloc_scratch_bytes() { return kDecodeNoAllocScratchBytes; }
+
+// The error word sits at offset 0 of every workspace layout, so it is the
+// array's first 4 bytes whatever the shape of the last call.
+int decode_noalloc_error_word(uint32_t** out) {
+  if (out == nullptr) return set_error(B200_ERR_INVALID, "error_word_out must not be NULL");
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch_address(&scratch);
+  if (rc != B200_OK) return rc;
+  *out = static_cast<uint32_t*>(scratch);
+  return B200_OK;
+}
 
 int launch_paged_decode_noalloc(const b200_cache_desc* c, const b200_decode_args* a,
                                 const void* query, const void* block_tables,

@@ -24,6 +24,7 @@ int launch_paged_decode_append(const b200_cache_desc* c, const b200_decode_args*
 
 // Allocation-free variant: split scratch from a static device array (decode.cu).
 size_t decode_noalloc_scratch_bytes();
+int decode_noalloc_error_word(uint32_t** out);
 int launch_paged_decode_noalloc(const b200_cache_desc* c, const b200_decode_args* a,
                                 const void* query, const void* block_tables,
                                 const void* context_lens, void* out, cudaStream_t stream);

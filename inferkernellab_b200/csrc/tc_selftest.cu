@@ -130,7 +130,62 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const uint16_t* a, con
   if (warp == 0) tc::tmem_dealloc(tbase, 512);
 }
 
+// Bounded-wait self-test: drives the give-up path of mbar_wait_bounded -- the
+// wait every kernel of this library uses on its mbarriers -- with a short
+// limit instead of the kernels' 1 s.  96 threads.  Warp 0 waits on an
+// mbarrier that expects one arrival; warp 1's first thread arrives only when
+// `arrive` is set; warp 2 waits with a limit four times longer, so when nobody
+// arrives it must leave through the CTA abort flag that warp 0 raises when it
+// gives up (the path every other waiter of an aborting kernel takes).  No copy
+// or MMA is in flight, so the kernel simply returns.
+//   result[0] = threads of warp 0 whose wait completed,
+//   result[1] = threads of warp 2 whose wait completed,
+//   result[2] = %globaltimer ns warp 0's first thread spent in its wait (capped).
+__global__ void __launch_bounds__(96) wait_selftest_kernel(unsigned long long limit_ns,
+                                                           int arrive, uint32_t* result,
+                                                           uint32_t* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  __shared__ uint32_t done[2];
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+    done[0] = done[1] = 0;
+  }
+  __syncthreads();
+  volatile int* abort = reinterpret_cast<volatile int*>(&abort_flag);
+  if (warp == 1) {
+    if (arrive && tid == 32) mbar_arrive(&bar);
+  } else {
+    const unsigned long long t0 = global_timer_ns();
+    const bool ok = mbar_wait_bounded(&bar, 0, abort, err, kErrWaitFull,
+                                      warp == 0 ? limit_ns : 4 * limit_ns);
+    const unsigned long long spent = global_timer_ns() - t0;
+    if (ok) atomicAdd(&done[warp == 0 ? 0 : 1], 1u);
+    if (tid == 0) result[2] = static_cast<uint32_t>(spent > 0xffffffffull ? 0xffffffffull : spent);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    result[0] = done[0];
+    result[1] = done[1];
+  }
+}
+
 }  // namespace
+
+int launch_wait_selftest(int64_t limit_ns, int32_t arrive, uint32_t* result, uint32_t* err,
+                         cudaStream_t stream) {
+  if (result == nullptr || err == nullptr)
+    return set_error(B200_ERR_INVALID, "result and error_word must not be NULL");
+  if (limit_ns < 1000 || limit_ns > 2000000000ll)
+    return set_error(B200_ERR_INVALID, "limit_ns must be within [1 us, 2 s]");
+  wait_selftest_kernel<<<1, 96, 0, stream>>>(static_cast<unsigned long long>(limit_ns),
+                                             arrive ? 1 : 0, result, err);
+  return cuda_status(cudaGetLastError(), "wait_selftest_kernel launch");
+}
 
 int launch_tc_selftest(const void* a, const void* b, const void* v, float* c1, float* c2,
                        float* c3, int32_t dtype, uint32_t* err, cudaStream_t stream) {

@@ -647,12 +647,26 @@ def correctness(model, prompts, result: LlamaPagedRunResult) -> dict:
             "oracle": "Transformers Llama eager full-sequence path"}
 
 
+def partition_requests(num_requests: int, world: int, rank: int) -> range:
+    """The contiguous slice of request indices rank ``rank`` of ``world`` serves.
+
+    Every rank gets ``ceil(num_requests / world)`` requests except the last
+    ones, which may get fewer (or none); each rank then runs its own runner with
+    its own block pool over ``prompts[slice]``.
+    """
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    per = -(-num_requests // world)
+    return range(min(rank * per, num_requests), min((rank + 1) * per, num_requests))
+
+
 def allgather_token_exchange(group=None, max_local: int | None = None) -> TokenExchange:
-    """NCCL all-gather of every rank's sampled token ids (one collective per decode step).
+    """All-gather of every rank's sampled token ids (one collective per decode step).
 
     Returns a callable for ``LlamaPagedDecodeRunner(token_exchange=...)``; the
     gathered ids of the last step are kept in ``callable.last`` (``[world, max_local]``,
-    ``-1`` = padding).
+    ``-1`` = padding).  The gather runs into a flat ``[world * max_local]``
+    buffer, the form every backend takes (NCCL on GPUs, gloo for host tests).
     """
     import torch.distributed as dist
 
@@ -663,10 +677,10 @@ def allgather_token_exchange(group=None, max_local: int | None = None) -> TokenE
         width = max_local or tokens.numel()
         local = torch.full((width,), -1, dtype=torch.int32, device=tokens.device)
         local[: tokens.numel()] = tokens.to(torch.int32)
-        if state["buf"] is None or state["buf"].shape[1] != width:
-            state["buf"] = torch.empty((world, width), dtype=torch.int32, device=tokens.device)
+        if state["buf"] is None or state["buf"].numel() != world * width:
+            state["buf"] = torch.empty((world * width,), dtype=torch.int32, device=tokens.device)
         dist.all_gather_into_tensor(state["buf"], local, group=group)
-        exchange.last = state["buf"]
+        exchange.last = state["buf"].view(world, width)
 
     exchange.last = None
     return exchange

@@ -27,4 +27,5 @@ from .paged_ref import (  # noqa: F401
     dense_decode_attention,
     paged_decode_attention,
     paged_prefill_attention,
+    paged_prefill_attention_packed,
 )

@@ -226,3 +226,46 @@ def paged_prefill_attention(query: np.ndarray, k_store: np.ndarray, v_store: np.
                 out[b, h, t] = probs @ vh[:limit]
     return out
 
+
+
+def paged_prefill_attention_packed(query: np.ndarray, k_store: np.ndarray, v_store: np.ndarray,
+                                   kind: str, block_tables, query_starts, context_lens,
+                                   scale: float | None = None, layer: int = 0) -> np.ndarray:
+    """The same causal prefill for a packed query ``[sum T, Hq, D]``, float32.
+
+    Sequence ``b`` owns the rows ``sum(T[:b]) .. sum(T[:b+1])-1``, its query
+    tokens of logical positions ``query_starts[b] .. context_lens[b]-1``; query
+    position ``p`` attends keys ``0..p`` (the unpadded rows of
+    ``paged_prefill_attention`` above, which follows reference
+    ``attention.py:230-321``).  Vectorised per (sequence, KV head) -- one masked
+    score matrix for the whole query-head group -- so full-size budget batches
+    finish in seconds; ``tests/test_oracle_golden.py`` holds it equal to the
+    loop form and to the reference's golden outputs.
+    """
+    q32 = to_f32(query, kind)
+    total, num_heads, head_dim = q32.shape
+    num_kv_heads = k_store.shape[3]
+    group = num_heads // num_kv_heads
+    scale = head_dim ** -0.5 if scale is None else scale
+    out = np.zeros_like(q32)
+    row = 0
+    for b in range(len(query_starts)):
+        start, end = int(query_starts[b]), int(context_lens[b])
+        length = end - start
+        if start < 0 or length <= 0:
+            raise ValueError("prefill ranges must be non-empty and non-negative")
+        if row + length > total:
+            raise ValueError("packed query holds fewer rows than the prefill ranges")
+        key = to_f32(read_tokens(k_store, layer, list(block_tables[b]), end), kind)
+        value = to_f32(read_tokens(v_store, layer, list(block_tables[b]), end), kind)
+        # visible[t, j]: query row t (position start + t) may attend key j
+        visible = np.arange(end)[None, :] <= (start + np.arange(length))[:, None]
+        for kv in range(num_kv_heads):
+            heads = slice(kv * group, (kv + 1) * group)
+            q = q32[row:row + length, heads, :]                      # [T, G, D]
+            scores = np.einsum("tgd,jd->gtj", q, key[:, kv, :]) * np.float32(scale)
+            scores = np.where(visible[None], scores, -np.inf).astype(np.float32)
+            probs = _softmax_rows(scores)
+            out[row:row + length, heads, :] = np.einsum("gtj,jd->tgd", probs, value[:, kv, :])
+        row += length
+    return out

@@ -106,3 +106,48 @@ def test_synthetic_decoder_oracle_matches_reference():
             np.testing.assert_allclose(got, np.asarray(want, np.float32), atol=2e-6, rtol=1e-5,
                                        err_msg=f"{name} step {step}")
             assert got.argmax(-1).tolist() == [g[step] for g in case["generated"]]
+
+
+def _pack_padded(query, query_starts, context_lens):
+    """[B, Hq, T, D] padded rows -> [sum T, Hq, D] packed rows (unpadded only)."""
+    rows = [query[b, :, :e - s, :].transpose(1, 0, 2)
+            for b, (s, e) in enumerate(zip(query_starts, context_lens))]
+    return np.concatenate(rows, axis=0)
+
+
+@pytest.mark.parametrize("path", sorted(GOLDEN.glob("prefill_*.npz")), ids=lambda p: p.stem)
+def test_packed_prefill_oracle_matches_reference_and_loop_form(path):
+    d = np.load(path)
+    starts, ends = d["query_starts"].tolist(), d["context_lens"].tolist()
+    packed = _pack_padded(d["query"], starts, ends)
+    got = oracle.paged_prefill_attention_packed(packed, d["k"], d["v"], str(d["kind"]),
+                                                d["block_tables"].tolist(), starts, ends)
+    want = _pack_padded(d["out_f32"], starts, ends)
+    np.testing.assert_allclose(got, want, atol=2e-6, rtol=2e-5)
+
+
+@pytest.mark.parametrize("kind,group", [("bf16", 4), ("f16", 1), ("bf16", 8)])
+def test_packed_prefill_oracle_matches_loop_form_on_ragged_chunks(kind, group):
+    rng = np.random.default_rng(7 + group)
+    hkv, dim, bs = 2, 32, 8
+    starts, ends = [0, 5, 30, 11], [9, 21, 47, 12]  # chunked ranges, one single-token range
+    need = [-(-e // bs) for e in ends]
+    nb = sum(need) + 3
+    perm = rng.permutation(nb).tolist()
+    tables, cur = [], 0
+    for n in need:
+        tables.append(perm[cur:cur + n] + [0] * (max(need) - n))
+        cur += n
+
+    def store(shape):
+        x = rng.standard_normal(shape, dtype=np.float32)
+        return oracle.f32_to_bf16_bits(x) if kind == "bf16" else x.astype(np.float16)
+
+    k = store((1, nb, bs, hkv, dim))
+    v = store((1, nb, bs, hkv, dim))
+    width = max(e - s for s, e in zip(starts, ends))
+    query = store((len(ends), hkv * group, width, dim))
+    loop = oracle.paged_prefill_attention(query, k, v, kind, tables, starts, ends, scale=0.3)
+    packed = oracle.paged_prefill_attention_packed(_pack_padded(query, starts, ends), k, v, kind,
+                                                   tables, starts, ends, scale=0.3)
+    np.testing.assert_allclose(packed, _pack_padded(loop, starts, ends), atol=2e-6, rtol=2e-5)

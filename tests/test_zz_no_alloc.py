@@ -4,9 +4,12 @@
 while attention runs (a plugin or custom operator inside a host framework that
 owns every buffer, or code held to a fixed memory budget): they pass inputs and
 outputs only, and the kernel's split scratch comes from the library's static
-8 MiB device array.  These tests check it against the workspace entry point
-(``b200_paged_decode`` via ``paged_decode_attention``) within the decode
-tolerances, on two calls in a row, and that an over-size shape is refused.
+8 MiB device array.  These tests check, on two calls in a row, that it gives
+exactly the workspace entry point's output (``b200_paged_decode`` via
+``paged_decode_attention``: same kernel, same grid), that both are within the
+decode tolerances of the float32 oracle, that the array's error word (read
+through ``b200_paged_decode_noalloc_error_word``) stays clear on valid input
+and reports a masked out-of-pool block, and that an over-size shape is refused.
 
 This file is collected last on purpose, and it passes both alone in a fresh
 process and after the rest of the suite.
@@ -19,13 +22,14 @@ import torch
 
 from inferkernellab_b200 import _lib, paged_decode_attention
 from inferkernellab_b200.ops import _cache_desc
-from tests.helpers import TOL, DecodeCase
+from tests.helpers import DecodeCase, assert_close
 
 pytestmark = pytest.mark.gpu
 
 
-def _noalloc(case: DecodeCase, out: torch.Tensor, scale: float) -> int:
-    query, tables, lens = case.query, case.tables, case.lens
+def _noalloc(case: DecodeCase, out: torch.Tensor, scale: float, tables=None) -> int:
+    query, lens = case.query, case.lens
+    tables = case.tables if tables is None else tables
     desc = _cache_desc(case.cache)
     args = _lib.DecodeArgs(query.shape[0], query.shape[1], tables.shape[1], case.layer,
                            query.stride(0), query.stride(1), out.stride(0), out.stride(1),
@@ -34,6 +38,20 @@ def _noalloc(case: DecodeCase, out: torch.Tensor, scale: float) -> int:
     return _lib.load().b200_paged_decode_noalloc(ctypes.byref(desc), ctypes.byref(args),
                                                  query.data_ptr(), tables.data_ptr(),
                                                  lens.data_ptr(), out.data_ptr(), stream)
+
+
+def _error_word() -> int:
+    """Reads (and clears) the static array's error word on the current device."""
+    lib = _lib.load()
+    addr = ctypes.c_void_p()
+    rc = lib.b200_paged_decode_noalloc_error_word(ctypes.byref(addr))
+    assert rc == _lib.B200_OK, _lib.last_error()
+    assert addr.value
+    value = ctypes.c_uint32(0)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = lib.b200_read_error_word(addr, ctypes.byref(value), 1, stream)
+    assert rc == _lib.B200_OK, _lib.last_error()
+    return value.value
 
 
 @pytest.mark.parametrize("shape", [
@@ -50,15 +68,30 @@ def test_noalloc_matches_workspace_entry_point_twice(shape):
                       lens=lens, dtype=dtype, seed=batch * 31 + dim)
     scale = dim ** -0.5
     want = paged_decode_attention(case.query, case.cache, case.tables, case.lens,
-                                  validate_inputs=False).float()
-    tol = TOL[dtype]
+                                  validate_inputs=False)
+    assert_close(want, case.oracle(), dtype, "workspace entry point vs oracle")
     for call in range(2):
         out = torch.full_like(case.query, float("nan"))
         rc = _noalloc(case, out, scale)
         assert rc == _lib.B200_OK, _lib.last_error()
-        torch.cuda.synchronize()
-        assert torch.allclose(out.float(), want, atol=tol["atol"], rtol=tol["rtol"]), \
-            f"call {call}: max |diff| {(out.float() - want).abs().max().item():.3e}"
+        assert _error_word() == 0, f"call {call}: device error word set"
+        assert torch.equal(out, want), \
+            f"call {call}: max |diff| {(out.float() - want.float()).abs().max().item():.3e}"
+        assert_close(out, case.oracle(), dtype, f"no-alloc call {call} vs oracle")
+
+
+def test_noalloc_reports_a_masked_block_through_its_error_word():
+    case = DecodeCase(batch=2, num_heads=32, num_kv_heads=8, head_dim=128, block_size=16,
+                      lens=[100, 40], dtype=torch.bfloat16, seed=11)
+    bad = case.tables.clone()
+    bad[1, 0] = case.cache.layout.num_blocks + 3  # outside the pool: masked, flagged
+    out = torch.empty_like(case.query)
+    assert _noalloc(case, out, 128 ** -0.5, tables=bad) == _lib.B200_OK, _lib.last_error()
+    assert _error_word() & _lib.DEVERR_BAD_BLOCK
+    # the next call starts from a clear word and request 0 is unaffected
+    assert _noalloc(case, out, 128 ** -0.5) == _lib.B200_OK, _lib.last_error()
+    assert _error_word() == 0
+    assert_close(out, case.oracle(), torch.bfloat16, "no-alloc after a flagged call")
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
