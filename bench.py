@@ -29,9 +29,12 @@ side streams against two device buffer sets, overlapping the neighbouring
 steps' kernels, as a serving loop overlaps them).  ``roofline`` is the
 step's kernel, timed with CUDA events around each of its launches.
 
-``--impl reference`` times the reference algorithm's CPU implementation (the
-numpy restatement in ``oracle/`` of the reference's ``paged_decode_attention``)
-on a bounded sample of the same workload, with all host threads.
+``--impl reference`` times the reference's own CPU implementation of the step
+-- ``PagedKVCache.write_slots`` + ``paged_decode_attention`` (the
+``paged_reference`` backend) of the reference project installed under
+``baseline/_ref`` -- on the same seed-0 batch copied to the host, with all host
+threads (the numpy restatement in ``oracle/`` stands in when that install is
+absent).  ``cpu_baseline`` is the same path on a bounded sample.
 
 Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): every rank owns
 its own 64-request batch and its own block pool (requests are partitioned by
@@ -42,7 +45,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import re
 import statistics
@@ -54,6 +56,8 @@ from pathlib import Path
 
 import numpy as np
 import torch
+
+from inferkernellab_b200.workloads import workload_lens, workload_tensors
 
 ROOT = Path(__file__).resolve().parent
 METRIC = "paged-decode-attn achieved HBM GB/s"
@@ -68,37 +72,21 @@ class Workload:
                  head_dim=128, block_size=16, max_ctx=8192, dtype=torch.bfloat16):
         from inferkernellab_b200 import PagedKVCache
 
+        t = workload_tensors(seed, device, batch, num_heads, num_kv_heads, head_dim, block_size,
+                             max_ctx, dtype)
         self.batch, self.num_heads, self.num_kv_heads = batch, num_heads, num_kv_heads
         self.head_dim, self.block_size, self.dtype = head_dim, block_size, dtype
-        lens = torch.tensor(workload_lens(seed, batch, max_ctx))
-        gen = torch.Generator().manual_seed(seed + 7)
-        need = (lens + block_size - 1) // block_size
-        num_blocks = int(math.ceil(1.1 * int(need.sum())))
-        perm = torch.randperm(num_blocks, generator=gen)
-        width = int(need.max())
-        tables = torch.zeros(batch, width, dtype=torch.int32)
-        cursor = 0
-        for b in range(batch):
-            n = int(need[b])
-            tables[b, :n] = perm[cursor:cursor + n].to(torch.int32)
-            cursor += n
-        self.lens_list = lens.tolist()
-        self.tables_host = tables
-        self.cache = PagedKVCache(num_blocks, block_size, num_kv_heads, head_dim, dtype=dtype,
+        self.lens_list = t["lens"]
+        self.tables_host = t["tables"]
+        self.cache = PagedKVCache(t["num_blocks"], block_size, num_kv_heads, head_dim, dtype=dtype,
                                   device=device)
-        dgen = torch.Generator(device=device).manual_seed(seed + 1)
-        self.cache.k.copy_(torch.randn(self.cache.k.shape, generator=dgen, device=device, dtype=dtype))
-        self.cache.v.copy_(torch.randn(self.cache.v.shape, generator=dgen, device=device, dtype=dtype))
-        self.query = torch.randn(batch, num_heads, head_dim, generator=dgen, device=device, dtype=dtype)
-        self.new_k = torch.randn(batch, num_kv_heads, head_dim, generator=dgen, device=device,
-                                 dtype=dtype)
-        self.new_v = torch.randn(batch, num_kv_heads, head_dim, generator=dgen, device=device,
-                                 dtype=dtype)
-        pos = lens - 1  # the new token is the last position of each context
-        slots = tables[torch.arange(batch), pos // block_size].long() * block_size + pos % block_size
-        self.slots_host = slots.to(torch.int32)
-        self.tables = tables.to(device)
-        self.lens = lens.to(torch.int32).to(device)
+        self.cache.k.copy_(t["k"])
+        self.cache.v.copy_(t["v"])
+        del t["k"], t["v"]
+        self.query, self.new_k, self.new_v = t["query"], t["new_k"], t["new_v"]
+        self.slots_host = t["slots"]
+        self.tables = t["tables"].to(device)
+        self.lens = torch.tensor(self.lens_list, dtype=torch.int32, device=device)
         self.slots = self.slots_host.to(device)
         self.out = torch.empty_like(self.query)
 
@@ -179,7 +167,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
                 "mem_mhz": statistics.median(mem) if mem else None, "mem_max_mhz": mem_max,
                 "reasons": sorted(reasons), "samples": len(sm),
-                "window": "nvidia-smi every 50 ms over warm-up + timed steps"}
+                "window": "nvidia-smi every 50 ms over a 1 s untimed soak of the step, the timed steps and the per-launch event pass"}
 
 
 # ------------------------------------------------------------------ helpers
@@ -244,8 +232,14 @@ def run_ours(args, world, rank, local) -> dict | None:
     dec_end = [torch.cuda.Event(enable_timing=True) for _ in range(k_steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        for _ in range(max(3, args.warmup // 4)):
-            wl.step()
+        # An untimed soak of at least a second inside the sampler's window, so
+        # that the clock record holds samples under load even when the timed
+        # region itself is a few milliseconds.
+        soak_end = time.perf_counter() + 1.0
+        while time.perf_counter() < soak_end:
+            for _ in range(64):
+                wl.step()
+            torch.cuda.synchronize(device)
         _barrier_sync(world)
         t0.record(stream)
         for i in range(k_steps):
@@ -380,19 +374,13 @@ def run_ours(args, world, rank, local) -> dict | None:
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
-        record["cpu_baseline"] = cpu_baseline(wl, budget_s=args.cpu_budget)
+        record["cpu_baseline"] = cpu_baseline(wl, budget_s=args.cpu_budget, seed=args.seed)
     return record
 
 
 def _bits(t: torch.Tensor) -> np.ndarray:
     """bfloat16 tensor -> numpy uint16 bit patterns (the oracle's bf16 storage)."""
     return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
-
-
-def workload_lens(seed: int, batch: int = 64, max_ctx: int = 8192) -> list[int]:
-    """The context lengths Workload(seed) draws (same generator, same order)."""
-    gen = torch.Generator().manual_seed(seed)
-    return torch.randint(1, max_ctx + 1, (batch,), generator=gen).tolist()
 
 
 def _oracle_sample_from(wl: Workload, max_tokens: int):
@@ -414,9 +402,9 @@ def _oracle_sample_from(wl: Workload, max_tokens: int):
             [wl.lens_list[b] for b in chosen])
 
 
-def _oracle_sample_host(seed: int, max_tokens: int, num_heads=32, num_kv_heads=8, head_dim=128,
-                        block_size=16):
-    """The same requests, generated on the host only (for the CPU reference arm)."""
+def _oracle_sample_from_host(seed: int, max_tokens: int, num_heads=32, num_kv_heads=8,
+                             head_dim=128, block_size=16):
+    """Leading requests of the config-3 batch with host-drawn values (numpy)."""
     lens_all = workload_lens(seed)
     lens, total = [], 0
     for n in lens_all:
@@ -458,9 +446,105 @@ def _time_oracle(q, k, v, tables, lens, threads: int) -> float:
     return time.perf_counter() - t
 
 
-def cpu_baseline(wl: Workload, budget_s: float) -> dict:
-    """The reference algorithm (numpy restatement) on host cores, bounded sample."""
+def _reference_package():
+    """The reference project installed under baseline/_ref, or (None, why)."""
+    path = ROOT / "baseline" / "_ref"
+    if not (path / "inferkernellab").is_dir():
+        return None, "baseline/_ref holds no reference install"
+    if str(path) not in sys.path:
+        sys.path.insert(0, str(path))
+    try:
+        from inferkernellab import attention, cache  # the reference's own modules
+    except Exception as exc:  # noqa: BLE001 -- any import failure means "not available"
+        return None, f"reference import failed: {type(exc).__name__}: {exc}"
+    return (attention, cache), ""
+
+
+class ReferenceStep:
+    """One config-3 step through the reference's own CPU path, on host tensors.
+
+    ``PagedKVCache.write_slots`` appends the new token of every request
+    (reference ``cache.py:156-189``), then ``paged_decode_attention`` -- the
+    reference's ``paged_reference`` backend, a per-request gather and a float32
+    dense attention (``attention.py:134-175``) -- attends over the whole context.
+    The inputs are the GPU arm's tensors of the same seed, copied to the host.
+    """
+
+    def __init__(self, modules, seed: int):
+        attention, cache_mod = modules
+        device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() \
+            else torch.device("cpu")
+        t = workload_tensors(seed, device)
+        self._all = dict(lens=t["lens"], tables=t["tables"], query=t["query"].cpu(),
+                         new_k=t["new_k"].cpu(), new_v=t["new_v"].cpu(), slots=t["slots"].cpu())
+        self.cache = cache_mod.PagedKVCache(t["num_blocks"], t["block_size"], t["num_kv_heads"],
+                                            t["head_dim"], dtype=t["dtype"], device="cpu")
+        self.cache.k.copy_(t["k"].cpu())
+        self.cache.v.copy_(t["v"].cpu())
+        del t
+        self.attention = attention
+        self.same_data = device.type == "cuda"
+        self.restrict(len(self._all["lens"]))
+
+    def restrict(self, requests: int) -> "ReferenceStep":
+        """Make a step cover the leading ``requests`` requests of the batch."""
+        a, n = self._all, requests
+        self.lens, self.tables, self.query = a["lens"][:n], a["tables"][:n], a["query"][:n]
+        self.new_k, self.new_v, self.slots = a["new_k"][:n], a["new_v"][:n], a["slots"][:n]
+        self.bytes = _oracle_bytes(self.lens) + 2 * 2 * n * 8 * 128 * 2 + n * 4
+        return self
+
+    def seconds_per_token(self) -> float:
+        """Times one step over the first 4 requests (warms the code path too)."""
+        n = len(self.lens)
+        self.restrict(4)
+        t = time.perf_counter()
+        self()
+        per_token = (time.perf_counter() - t) / max(1, sum(self.lens))
+        self.restrict(n)
+        return per_token
+
+    def __call__(self):
+        self.cache.write_slots(0, self.slots, self.new_k, self.new_v)
+        return self.attention.paged_decode_attention(self.query, self.cache, self.tables,
+                                                     self.lens)
+
+
+def _reference_requests(seed: int, budget_s: float, per_step_probe) -> int:
+    """How many leading requests of the batch fit in ``budget_s`` per step."""
+    lens = workload_lens(seed)
+    per_token = per_step_probe
+    total, n = 0, 0
+    for length in lens:
+        if n and (total + length) * per_token > budget_s:
+            break
+        total += length
+        n += 1
+    return n
+
+
+def cpu_baseline(wl: Workload, budget_s: float, seed: int) -> dict:
+    """The reference's own CPU path (baseline/_ref) on host cores, bounded sample.
+
+    Falls back to the numpy restatement in ``oracle/`` (``kind: "port"``) when
+    the reference install is absent.
+    """
     threads = os.cpu_count() or 1
+    modules, why = _reference_package()
+    if modules is not None:
+        torch.set_num_threads(threads)
+        step = ReferenceStep(modules, seed)
+        n = _reference_requests(seed, budget_s, step.seconds_per_token())
+        step.restrict(n)
+        t = time.perf_counter()
+        step()
+        secs = time.perf_counter() - t
+        return {"value": round(step.bytes / secs / 1e9, 4), "unit": "GB/s",
+                "cores": torch.get_num_threads(), "kind": "reference",
+                "sample": f"first {n} of the 64 requests of rank 0 ({sum(step.lens)} context "
+                          f"tokens): the reference's write_slots + paged_decode_attention "
+                          f"(baseline/_ref, torch CPU, bf16 cache, fp32 math), "
+                          f"{torch.get_num_threads()} threads, {secs:.2f} s"}
     q, k, v, tables, lens = _oracle_sample_from(wl, max_tokens=4096)
     probe = _time_oracle(q, k, v, tables, lens, threads)
     per_token = probe / max(1, sum(lens))
@@ -471,35 +555,65 @@ def cpu_baseline(wl: Workload, budget_s: float) -> dict:
     return {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"first {len(lens)} of the 64 requests of rank 0 ({sum(lens)} context "
                       f"tokens), numpy float32 restatement of paged_decode_attention, "
-                      f"{threads} threads, {secs:.2f} s"}
+                      f"{threads} threads, {secs:.2f} s ({why})"}
 
 
 def run_reference(args, world, rank) -> dict | None:
-    """CPU reference arm: the reference algorithm on host cores, same metric and config."""
+    """CPU reference arm: the reference's own CPU path, same metric and config.
+
+    With the reference installed under baseline/_ref, every step is
+    ``write_slots`` + ``paged_decode_attention`` of the reference itself on the
+    GPU arm's seed-0 batch (the whole batch when warm-up + steps fit in about
+    two minutes, else its leading requests); without it, the numpy
+    restatement of the same algorithm.  Rank 0 alone runs it.
+    """
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
-    probe = _oracle_sample_host(args.seed, max_tokens=2048)
-    per_token = _time_oracle(*probe, threads) / max(1, sum(probe[4]))
-    # Size each step so that warm-up + steps end within about two minutes.
-    per_step_s = 120.0 / (args.steps + min(args.warmup, 3))
-    tokens = int(min(8192 * 4, max(64, per_step_s / max(per_token, 1e-9))))
-    q, k, v, tables, lens = _oracle_sample_host(args.seed, max_tokens=tokens)
-    for _ in range(min(args.warmup, 3)):
-        _time_oracle(q, k, v, tables, lens, threads)
-    secs = [_time_oracle(q, k, v, tables, lens, threads) for _ in range(args.steps)]
+    warm = min(args.warmup, 3)
+    per_step_s = 120.0 / (args.steps + warm)
+    modules, why = _reference_package()
+    if modules is not None:
+        torch.set_num_threads(threads)
+        step = ReferenceStep(modules, args.seed)
+        n = _reference_requests(args.seed, per_step_s, step.seconds_per_token())
+        step.restrict(n)
+        for _ in range(warm):
+            step()
+        secs = []
+        for _ in range(args.steps):
+            t = time.perf_counter()
+            step()
+            secs.append(time.perf_counter() - t)
+        kind, cores, step_bytes = "reference", torch.get_num_threads(), step.bytes
+        same = n == 64 and step.same_data
+        sample = (f"{'all' if n == 64 else f'first {n} of the'} 64 requests of the config-3 "
+                  f"batch ({sum(step.lens)} context tokens{'' if step.same_data else ', CPU-drawn values'}) per step: "
+                  f"the reference's PagedKVCache.write_slots + paged_decode_attention "
+                  f"(baseline/_ref, torch CPU, bf16 cache, fp32 math), {cores} threads")
+    else:
+        q, k, v, tables, lens = _oracle_sample_from_host(args.seed, max_tokens=2048)
+        per_token = _time_oracle(q, k, v, tables, lens, threads) / max(1, sum(lens))
+        tokens = int(min(8192 * 4, max(64, per_step_s / max(per_token, 1e-9))))
+        q, k, v, tables, lens = _oracle_sample_from_host(args.seed, max_tokens=tokens)
+        for _ in range(warm):
+            _time_oracle(q, k, v, tables, lens, threads)
+        secs = [_time_oracle(q, k, v, tables, lens, threads) for _ in range(args.steps)]
+        kind, cores, step_bytes, same = "port", threads, _oracle_bytes(lens), False
+        sample = (f"first {len(lens)} requests of the config-3 batch ({sum(lens)} context "
+                  f"tokens) per step, numpy float32 restatement of the reference "
+                  f"paged_decode_attention, {threads} threads ({why})")
     total = sum(secs)
-    gbs = _oracle_bytes(lens) * len(secs) / total / 1e9
-    sample = (f"first {len(lens)} requests of the config-3 batch ({sum(lens)} context tokens) per "
-              f"step, numpy float32 restatement of the reference paged_decode_attention, "
-              f"{threads} threads")
+    gbs = step_bytes * len(secs) / total / 1e9
     return {
         "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / len(secs) * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "impl": "reference", "config": {"workload": WORKLOAD, "sample": sample},
-        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+        "impl": "reference",
+        "config": {"workload": WORKLOAD, "sample": sample, "same_config": same,
+                   "seed": args.seed},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": kind,
                          "sample": sample},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
