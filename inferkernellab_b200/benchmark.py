@@ -38,6 +38,7 @@ from . import _lib
 from .cache import PagedKVCache
 from .ops import (
     append_kv,
+    rope_append_kv,
     paged_decode_attention,
     paged_decode_attention_append,
     paged_prefill_attention_varlen,
@@ -290,26 +291,38 @@ def run_prefill(args) -> dict:
         k = torch.randn(total, hkv, dim, device=device, dtype=dtype)
         v = torch.randn(total, hkv, dim, device=device, dtype=dtype)
         btab = tables[ids].contiguous()
-        work.append((btab, starts, ends, total, q, k, v))
+        rot = None
+        if args.rope:  # Llama-3 rotary rows (theta 5e5) of every scheduled position
+            pos = torch.tensor([t for _, s, e in batch for t in range(s, e)], dtype=torch.float64)
+            inv = 1.0 / (5e5 ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
+            ang = pos[:, None] * inv[None, :]
+            emb = torch.cat((ang, ang), dim=-1)
+            rot = (emb.cos().to(dtype).to(device), emb.sin().to(dtype).to(device),
+                   torch.empty_like(q))
+        work.append((btab, starts, ends, total, q, k, v, rot))
         for _, s, e in batch:
             flops += sum(2.0 * 2.0 * dim * hq * (p + 1) for p in range(s, e))
 
     def step():
-        for btab, starts, ends, total, q, k, v in work:
+        for btab, starts, ends, total, q, k, v, rot in work:
             slots, cu = build_slot_mapping(btab, starts, ends, block_size=bs,
                                            num_blocks=num_blocks, total_tokens=total)
-            append_kv(k, v, cache, slots)
-            paged_prefill_attention_varlen(q, cache, btab, cu, starts, ends,
+            if rot is None:
+                append_kv(k, v, cache, slots)
+                qr = q
+            else:
+                qr = rope_append_kv(q, k, v, rot[0], rot[1], cache, slots, out=rot[2])
+            paged_prefill_attention_varlen(qr, cache, btab, cu, starts, ends,
                                            kernel=args.prefill_kernel)
 
     metas = []
-    for btab, starts, ends, total, q, k, v in work:
+    for btab, starts, ends, total, q, k, v, rot in work:
         slots, cu = build_slot_mapping(btab, starts, ends, block_size=bs,
                                        num_blocks=num_blocks, total_tokens=total)
         metas.append(cu)
 
     def attention_only():
-        for (btab, starts, ends, total, q, k, v), cu in zip(work, metas):
+        for (btab, starts, ends, total, q, k, v, rot), cu in zip(work, metas):
             paged_prefill_attention_varlen(q, cache, btab, cu, starts, ends,
                                            kernel=args.prefill_kernel)
 
@@ -327,16 +340,32 @@ def run_prefill(args) -> dict:
 
     ms = timed(step)
     attn_ms = timed(attention_only)
+    # The same launches replayed from a CUDA graph: device time without the
+    # host's per-launch cost (the eager figures above include it when the host
+    # is slower than the kernels).
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        attention_only()
+    side.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        attention_only()
+    torch.cuda.current_stream(device).wait_stream(side)
+    attn_graph_ms = timed(graph.replay)
     return {
         "schema_version": 2, "benchmark": "config4_prefill",
         "environment": _environment(device),
         "config": {"prompts": lens, "budget": 2048, "batches": len(batches), "num_heads": hq,
                    "num_kv_heads": hkv, "head_dim": dim, "block_size": bs, "dtype": "bfloat16",
-                   "kernel": args.prefill_kernel},
+                   "kernel": args.prefill_kernel,
+                   "append": "rope_append_kv" if args.rope else "append_kv"},
         "prefill_ms": ms, "causal_attention_flops": flops,
         "achieved_tflops": flops / (ms * 1e-3) / 1e12,
         "attention_only_ms": attn_ms,
         "attention_only_tflops": flops / (attn_ms * 1e-3) / 1e12,
+        "attention_graph_ms": attn_graph_ms,
+        "attention_graph_tflops": flops / (attn_graph_ms * 1e-3) / 1e12,
         "tokens_per_s": sum(lens) / (ms * 1e-3),
     }
 
@@ -466,6 +495,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--prefill-prompts", type=int, default=24)
     p.add_argument("--prefill-min-len", type=int, default=17)
     p.add_argument("--prefill-max-len", type=int, default=512)
+    p.add_argument("--rope", action="store_true",
+                   help="with --prefill: rotary + append in one rope_append_kv launch per batch")
     p.add_argument("--profile-kernel", action="store_true",
                    help="one decode launch between cudaProfilerStart/Stop (ncu --profile-from-start off)")
     p.add_argument("--reference-gpu", action="store_true",

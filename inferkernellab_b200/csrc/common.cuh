@@ -220,6 +220,22 @@ __device__ __forceinline__ uint32_t pack2<BF16>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Multiply both 16-bit values of a packed pair by `a` (rounded back to E).
+template <typename E>
+__device__ __forceinline__ uint32_t scale_pack2(uint32_t v, float a);
+
+template <>
+__device__ __forceinline__ uint32_t scale_pack2<Half>(uint32_t v, float a) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v));
+  return pack2<Half>(f.x * a, f.y * a);
+}
+
+template <>
+__device__ __forceinline__ uint32_t scale_pack2<BF16>(uint32_t v, float a) {
+  const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+  return pack2<BF16>(f.x * a, f.y * a);
+}
+
 template <typename E>
 __device__ __forceinline__ typename E::T from_float(float x);
 template <>

@@ -38,6 +38,41 @@ struct MapKeyHash {
   }
 };
 std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// Key of a general 16-bit tiled map (encode_tensor_map_16b).
+struct GenKey {
+  const void* base;
+  int rank, dtype;
+  uint64_t dims[5], strides[4];
+  uint32_t box[5];
+  bool operator==(const GenKey& o) const {
+    return base == o.base && rank == o.rank && dtype == o.dtype &&
+           std::memcmp(dims, o.dims, sizeof(dims)) == 0 &&
+           std::memcmp(strides, o.strides, sizeof(strides)) == 0 &&
+           std::memcmp(box, o.box, sizeof(box)) == 0;
+  }
+};
+struct GenKeyHash {
+  size_t operator()(const GenKey& k) const {
+    size_t h = std::hash<const void*>()(k.base) ^ (static_cast<size_t>(k.rank) << 3);
+    for (int i = 0; i < 5; ++i) h = h * 1000003u ^ std::hash<uint64_t>()(k.dims[i]);
+    for (int i = 0; i < 4; ++i) h = h * 1000003u ^ std::hash<uint64_t>()(k.strides[i]);
+    for (int i = 0; i < 5; ++i) h = h * 1000003u ^ k.box[i];
+    return h ^ static_cast<size_t>(k.dtype);
+  }
+};
+std::unordered_map<GenKey, CUtensorMap, GenKeyHash> g_gen_maps;
+
+int load_encoder() {
+  if (g_encode != nullptr) return B200_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (err != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+    return set_error(B200_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return B200_OK;
+}
 }  // namespace
 
 int set_error(int code, const std::string& msg) {
@@ -122,14 +157,8 @@ int encode_cache_tensor_map(const b200_cache_desc* c, const void* base,
     *out = it->second;
     return B200_OK;
   }
-  if (g_encode == nullptr) {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    cudaError_t err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-    if (err != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
-      return set_error(B200_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
-    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  }
+  const int enc = load_encoder();
+  if (enc != B200_OK) return enc;
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
     return set_error(B200_ERR_INVALID, "cache tensor base must be 16-byte aligned");
   cuuint64_t gdim[3] = {static_cast<cuuint64_t>(c->head_dim),
@@ -173,6 +202,61 @@ int encode_cache_tensor_map(const b200_cache_desc* c, const void* base,
                          ")");
   if (g_maps.size() > 4096) g_maps.clear();
   g_maps.emplace(key, map);
+  *out = map;
+  return B200_OK;
+}
+
+int encode_tensor_map_16b(const void* base, int rank, const uint64_t* dims,
+                          const uint64_t* strides_bytes, const uint32_t* box, int dtype,
+                          CUtensorMap* out) {
+  if (rank < 2 || rank > 5) return set_error(B200_ERR_INVALID, "tensor map rank must be 2..5");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return set_error(B200_ERR_INVALID, "tensor base must be 16-byte aligned");
+  GenKey key{};
+  key.base = base;
+  key.rank = rank;
+  key.dtype = dtype;
+  for (int i = 0; i < rank; ++i) {
+    key.dims[i] = dims[i];
+    key.box[i] = box[i];
+    if (i + 1 < rank) {
+      key.strides[i] = strides_bytes[i];
+      if (strides_bytes[i] % 16 != 0)
+        return set_error(B200_ERR_INVALID, "tensor strides must be multiples of 16 bytes");
+    }
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  auto it = g_gen_maps.find(key);
+  if (it != g_gen_maps.end()) {
+    *out = it->second;
+    return B200_OK;
+  }
+  const int enc = load_encoder();
+  if (enc != B200_OK) return enc;
+  cuuint64_t gdim[5];
+  cuuint64_t gstride[4];
+  cuuint32_t gbox[5], estride[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = static_cast<cuuint64_t>(dims[i]);
+    gbox[i] = static_cast<cuuint32_t>(box[i]);
+    estride[i] = 1u;
+    if (i + 1 < rank) gstride[i] = static_cast<cuuint64_t>(strides_bytes[i]);
+  }
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  const CUresult r = g_encode(&map,
+                              dtype == B200_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              static_cast<cuuint32_t>(rank), const_cast<void*>(base), gdim, gstride,
+                              gbox, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(B200_ERR_CUDA,
+                     "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) +
+                         ")");
+  if (g_gen_maps.size() > 4096) g_gen_maps.clear();
+  g_gen_maps.emplace(key, map);
   *out = map;
   return B200_OK;
 }

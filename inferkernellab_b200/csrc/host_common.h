@@ -58,6 +58,13 @@ bool cache_head_group_geometry(const b200_cache_desc* cache, int heads, CacheTma
 int encode_cache_tensor_map(const b200_cache_desc* cache, const void* base,
                             const CacheTmaGeometry& geo, CUtensorMap* out);
 
+// Encodes (or returns a cached copy of) a tiled map of 16-bit elements with
+// 128-byte swizzle: `rank` dims innermost first, byte strides of dims
+// 1..rank-1 (multiples of 16), box sizes per dim.
+int encode_tensor_map_16b(const void* base, int rank, const uint64_t* dims,
+                          const uint64_t* strides_bytes, const uint32_t* box, int dtype,
+                          CUtensorMap* out);
+
 inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // Launch with programmatic stream serialization: the grid may be scheduled while

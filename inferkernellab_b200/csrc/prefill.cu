@@ -345,6 +345,7 @@ int launch_paged_prefill(const b200_cache_desc* c, const b200_prefill_args* a, c
   p.o_stride_token = a->o_stride_token;
   p.num_seqs = a->num_seqs;
   p.group = a->num_q_heads / c->num_kv_heads;
+  p.num_kv_heads = c->num_kv_heads;
   p.packed = a->query_layout;
   p.max_query_len = a->max_query_len;
   p.index64 = a->index_dtype == B200_I64;
@@ -360,25 +361,54 @@ int launch_paged_prefill(const b200_cache_desc* c, const b200_prefill_args* a, c
   const long long row_bits = a->q_stride_head | a->q_stride_token | a->o_stride_head |
                              a->o_stride_token |
                              (a->query_layout == 0 ? (a->q_stride_seq | a->o_stride_seq) : 0);
-  const bool tc_ok = (c->head_dim == 64 || c->head_dim == 128) && geo.swizzle_bytes == 128 &&
+  const bool pow2_group = (p.group & (p.group - 1)) == 0;
+  const bool tc_ok = (c->head_dim == 64 || c->head_dim == 128) && p.group <= 64 && pow2_group &&
+                     a->scale > 0.f &&
+                     geo.swizzle_bytes == 128 &&
                      geo.chunk_bytes == 128 && (row_bits & 7) == 0 &&
                      ((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
   if (a->kernel == B200_PREFILL_TCGEN05 && !tc_ok)
     return set_error(B200_ERR_UNSUPPORTED,
-                     "tcgen05 prefill needs head_dim 64/128, block_size >= 8 and 16-byte aligned "
+                     "tcgen05 prefill needs head_dim 64/128, block_size >= 8, a power-of-two number "
+                     "(<= 64) of query heads per kv head, a positive scale and 16-byte aligned "
                      "query/output rows");
   if (tc_ok && a->kernel != B200_PREFILL_MMA_SYNC) {
-    long long tx;
+    const int qb = prefill_tc_query_block(p.group);
+    long long items;
     if (a->query_layout == 0) {
-      tx = static_cast<long long>(a->num_seqs) * ((a->max_query_len + kTcRows - 1) / kTcRows);
+      items = static_cast<long long>(a->num_seqs) * ((a->max_query_len + qb - 1) / qb);
     } else {
       if (a->total_query_tokens <= 0) return B200_OK;
-      tx = (a->total_query_tokens + kTcRows - 1) / kTcRows + a->num_seqs;
+      items = (a->total_query_tokens + qb - 1) / qb + a->num_seqs;
     }
+    const long long tx = items * c->num_kv_heads;
     if (tx > 0x7fffffffLL) return set_error(B200_ERR_UNSUPPORTED, "prefill grid too large");
-    return launch_prefill_tc(kmap, vmap, p, c->head_dim, c->dtype == B200_BF16,
-                             static_cast<unsigned>(tx), static_cast<unsigned>(a->num_q_heads),
-                             stream);
+    // The query's TMA map: box {64 elements, heads per tile, tokens per tile}.
+    const uint32_t ht = static_cast<uint32_t>(prefill_tc_query_heads_per_tile(p.group));
+    const uint32_t tpt = static_cast<uint32_t>(kTcRows) / ht;
+    CUtensorMap qmap;
+    if (a->query_layout == 1) {
+      const uint64_t dims[3] = {static_cast<uint64_t>(c->head_dim),
+                                static_cast<uint64_t>(a->num_q_heads),
+                                static_cast<uint64_t>(a->total_query_tokens)};
+      const uint64_t strides[2] = {static_cast<uint64_t>(a->q_stride_head) * 2,
+                                   static_cast<uint64_t>(a->q_stride_token) * 2};
+      const uint32_t box[3] = {64u, ht, tpt};
+      rc = encode_tensor_map_16b(query, 3, dims, strides, box, c->dtype, &qmap);
+    } else {
+      const uint64_t dims[4] = {static_cast<uint64_t>(c->head_dim),
+                                static_cast<uint64_t>(a->num_q_heads),
+                                static_cast<uint64_t>(a->max_query_len),
+                                static_cast<uint64_t>(a->num_seqs)};
+      const uint64_t strides[3] = {static_cast<uint64_t>(a->q_stride_head) * 2,
+                                   static_cast<uint64_t>(a->q_stride_token) * 2,
+                                   static_cast<uint64_t>(a->q_stride_seq) * 2};
+      const uint32_t box[4] = {64u, ht, tpt, 1u};
+      rc = encode_tensor_map_16b(query, 4, dims, strides, box, c->dtype, &qmap);
+    }
+    if (rc != B200_OK) return rc;
+    return launch_prefill_tc(kmap, vmap, qmap, p, c->head_dim, c->dtype == B200_BF16,
+                             static_cast<unsigned>(tx), 1u, stream);
   }
 
   long long gx;

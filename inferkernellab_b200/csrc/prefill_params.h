@@ -22,19 +22,29 @@ struct PrefillParams {
   long long q_stride_seq, q_stride_head, q_stride_token;
   long long o_stride_seq, o_stride_head, o_stride_token;
   int num_seqs, group, packed, max_query_len, index64;
+  int num_kv_heads;
   int table_width;
   int sw_mask;
   float scale_log2;
 };
 
-// Query tokens per CTA of the tcgen05 kernel (one UMMA M tile).
+// Rows of one tcgen05 query tile (one UMMA M tile).
 constexpr int kTcRows = 128;
 
+// Query tokens per CTA of the tcgen05 kernel for `group` query heads per kv
+// head: the CTA's 256 rows are group heads x (256 / group) tokens.
+int prefill_tc_query_block(int group);
+// Query heads per 128-row tile of the tcgen05 kernel (the Q box's head extent).
+int prefill_tc_query_heads_per_tile(int group);
+
 // tcgen05 prefill: head_dim 64 or 128, cache tiles with 128-byte swizzle,
-// 16-byte aligned query/output rows.  `grid_x` counts 128-row query tiles
-// (packed: an upper bound, excess CTAs exit).
-int launch_prefill_tc(const CUtensorMap& kmap, const CUtensorMap& vmap, const PrefillParams& p,
-                      int head_dim, bool bf16, unsigned grid_x, unsigned grid_y,
-                      cudaStream_t stream);
+// 16-byte aligned query/output rows, a power-of-two number (<= 64) of query
+// heads per kv head.  `qmap` is the query tensor's TMA map with box {64,
+// heads per tile, 128 / heads per tile tokens (, 1)}: rank 3 {D, Hq, rows}
+// when packed, rank 4 {D, Hq, T, B} when padded.  `grid_x` = query blocks x
+// kv heads (packed: an upper bound on the blocks, excess CTAs exit); grid_y = 1.
+int launch_prefill_tc(const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensorMap& qmap,
+                      const PrefillParams& p, int head_dim, bool bf16, unsigned grid_x,
+                      unsigned grid_y, cudaStream_t stream);
 
 }  // namespace b200
