@@ -386,28 +386,35 @@ int launch_paged_prefill(const b200_cache_desc* c, const b200_prefill_args* a, c
     // The query's TMA map: box {64 elements, heads per tile, tokens per tile}.
     const uint32_t ht = static_cast<uint32_t>(prefill_tc_query_heads_per_tile(p.group));
     const uint32_t tpt = static_cast<uint32_t>(kTcRows) / ht;
-    CUtensorMap qmap;
-    if (a->query_layout == 1) {
-      const uint64_t dims[3] = {static_cast<uint64_t>(c->head_dim),
-                                static_cast<uint64_t>(a->num_q_heads),
-                                static_cast<uint64_t>(a->total_query_tokens)};
-      const uint64_t strides[2] = {static_cast<uint64_t>(a->q_stride_head) * 2,
-                                   static_cast<uint64_t>(a->q_stride_token) * 2};
-      const uint32_t box[3] = {64u, ht, tpt};
-      rc = encode_tensor_map_16b(query, 3, dims, strides, box, c->dtype, &qmap);
-    } else {
-      const uint64_t dims[4] = {static_cast<uint64_t>(c->head_dim),
-                                static_cast<uint64_t>(a->num_q_heads),
-                                static_cast<uint64_t>(a->max_query_len),
-                                static_cast<uint64_t>(a->num_seqs)};
-      const uint64_t strides[3] = {static_cast<uint64_t>(a->q_stride_head) * 2,
-                                   static_cast<uint64_t>(a->q_stride_token) * 2,
-                                   static_cast<uint64_t>(a->q_stride_seq) * 2};
-      const uint32_t box[4] = {64u, ht, tpt, 1u};
-      rc = encode_tensor_map_16b(query, 4, dims, strides, box, c->dtype, &qmap);
+    // The query's and the output's TMA maps: box {64 elements, heads per tile,
+    // tokens per tile (, 1 sequence)}.
+    CUtensorMap qmap, omap;
+    for (int which = 0; which < 2 && rc == B200_OK; ++which) {
+      const void* base = which == 0 ? query : out;
+      const int64_t sh = which == 0 ? a->q_stride_head : a->o_stride_head;
+      const int64_t st = which == 0 ? a->q_stride_token : a->o_stride_token;
+      const int64_t ss = which == 0 ? a->q_stride_seq : a->o_stride_seq;
+      CUtensorMap* dst = which == 0 ? &qmap : &omap;
+      if (a->query_layout == 1) {
+        const uint64_t dims[3] = {static_cast<uint64_t>(c->head_dim),
+                                  static_cast<uint64_t>(a->num_q_heads),
+                                  static_cast<uint64_t>(a->total_query_tokens)};
+        const uint64_t strides[2] = {static_cast<uint64_t>(sh) * 2, static_cast<uint64_t>(st) * 2};
+        const uint32_t box[3] = {64u, ht, tpt};
+        rc = encode_tensor_map_16b(base, 3, dims, strides, box, c->dtype, dst);
+      } else {
+        const uint64_t dims[4] = {static_cast<uint64_t>(c->head_dim),
+                                  static_cast<uint64_t>(a->num_q_heads),
+                                  static_cast<uint64_t>(a->max_query_len),
+                                  static_cast<uint64_t>(a->num_seqs)};
+        const uint64_t strides[3] = {static_cast<uint64_t>(sh) * 2, static_cast<uint64_t>(st) * 2,
+                                     static_cast<uint64_t>(ss) * 2};
+        const uint32_t box[4] = {64u, ht, tpt, 1u};
+        rc = encode_tensor_map_16b(base, 4, dims, strides, box, c->dtype, dst);
+      }
     }
     if (rc != B200_OK) return rc;
-    return launch_prefill_tc(kmap, vmap, qmap, p, c->head_dim, c->dtype == B200_BF16,
+    return launch_prefill_tc(kmap, vmap, qmap, omap, p, c->head_dim, c->dtype == B200_BF16,
                              static_cast<unsigned>(tx), 1u, stream);
   }
 

@@ -41,10 +41,11 @@ int prefill_tc_query_heads_per_tile(int group);
 // 16-byte aligned query/output rows, a power-of-two number (<= 64) of query
 // heads per kv head.  `qmap` is the query tensor's TMA map with box {64,
 // heads per tile, 128 / heads per tile tokens (, 1)}: rank 3 {D, Hq, rows}
-// when packed, rank 4 {D, Hq, T, B} when padded.  `grid_x` = query blocks x
-// kv heads (packed: an upper bound on the blocks, excess CTAs exit); grid_y = 1.
+// when packed, rank 4 {D, Hq, T, B} when padded; `omap` the same over the
+// output.  `grid_x` = query blocks x kv heads (packed: an upper bound on the
+// blocks, excess CTAs exit); grid_y = 1.
 int launch_prefill_tc(const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensorMap& qmap,
-                      const PrefillParams& p, int head_dim, bool bf16, unsigned grid_x,
-                      unsigned grid_y, cudaStream_t stream);
+                      const CUtensorMap& omap, const PrefillParams& p, int head_dim, bool bf16,
+                      unsigned grid_x, unsigned grid_y, cudaStream_t stream);
 
 }  // namespace b200

@@ -50,9 +50,7 @@
 #include "tcgen05.cuh"
 
 namespace b200 {
-
 namespace {
-
 constexpr int kFaTiles = 2;                       // query tiles per CTA
 constexpr int kFaKeys = 2 * kKvTile;              // keys per K/V stage
 constexpr int kFaProducerWarp = 8;
@@ -116,7 +114,8 @@ template <typename E, int D>
 __global__ void __launch_bounds__(kFaThreads, 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap,
-                            const __grid_constant__ CUtensorMap qmap, const PrefillParams p) {
+                            const __grid_constant__ CUtensorMap qmap,
+                            const __grid_constant__ CUtensorMap omap, const PrefillParams p) {
   using S = FaShape<D>;
   using T = typename E::T;
   constexpr int kStages = S::kStages;
@@ -559,9 +558,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         ok && n_kt > 0 &&
         warp_wait(&pv_done[x], static_cast<uint32_t>((n_kt - 1) & 1), abort_flag, p.err,
                   kErrWaitFull);
-    // O row / l -> this tile's Q buffer (free: every S MMA has finished), row r
-    // at r * 2D bytes with its 16-byte chunks XOR-swizzled by the row, then
-    // the tile's 128 threads copy the rows out coalesced.
+    // O row / l -> this tile's Q buffer (free: every S MMA has finished) in the
+    // Q box's layout (row r, 128-byte swizzle).  A tile whose rows all have
+    // output leaves as TMA stores of that box (one thread, asynchronous); the
+    // others are copied out by the tile's threads, coalesced, row by row.
     uint8_t* stg = q_s + x * S::kQTileBytes;
     if (have_o) {
       tc::fence_after_sync();
@@ -579,9 +579,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           v.z = pack2<E>(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
           v.w = pack2<E>(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
           const int chunk = cb * 4 + c;
-          *reinterpret_cast<uint4*>(stg + r * (D * 2) + ((chunk ^ (r % kChunks)) << 4)) = v;
+          *reinterpret_cast<uint4*>(stg + (chunk >> 3) * S::kQRegionBytes +
+                                    tc::sw128_offset(r, chunk & 7)) = v;
         }
       }
+      tc::fence_proxy_async_smem();  // the staged rows -> the TMA store
     }
     // Every thread of the tile reaches this barrier, whatever happened above;
     // the rows are copied out only when all 128 were staged.
@@ -594,7 +596,29 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         : "=r"(all_staged)
         : "r"(have_o ? 1u : 0u), "r"(2 + x), "n"(kTcRows)
         : "memory");
-    if (all_staged) {
+    // Rows with output: tokens below len_b (packed), or below the padded width
+    // when the context is not empty (padding rows attend key 0).
+    const long long valid_end = key_end <= 0 ? 0 : (p.packed ? len_b : max(len_b, rows_here));
+    const long long tile_t0 = t0 + (G >= 2 ? 0 : x * kTcRows);
+    const int tile_tokens = G >= 2 ? (kTcRows >> lg_ht) : kTcRows;
+    const bool tile_full = G >= 2 ? tile_t0 + tile_tokens <= valid_end && G == 2 * HT
+                                  : tile_t0 + tile_tokens <= valid_end;
+    if (all_staged && tile_full) {
+      if (r == 0) {
+        const int head0 = hk * G + (G >= 2 ? x * HT : 0);
+#pragma unroll
+        for (int c = 0; c < S::kRegions; ++c) {
+          if (p.packed)
+            tma_store_3d(&omap, stg + c * S::kQRegionBytes, c * 64, head0,
+                         static_cast<int>(q_row0 + tile_t0));
+          else
+            tma_store_4d(&omap, stg + c * S::kQRegionBytes, c * 64, head0,
+                         static_cast<int>(tile_t0), b);
+        }
+        bulk_commit_group();
+        bulk_wait_group_read0();  // the staging buffer is read before the CTA exits
+      }
+    } else if (all_staged) {
 #pragma unroll 4
       for (int it = 0; it < kCopies; ++it) {
         const int idx = it * kTcRows + r;
@@ -607,8 +631,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           T* base = reinterpret_cast<T*>(p.out);
           T* orow = p.packed ? base + (q_row0 + t) * p.o_stride_token + h * p.o_stride_head
                              : base + b * p.o_stride_seq + h * p.o_stride_head + t * p.o_stride_token;
-          reinterpret_cast<uint4*>(orow)[c] =
-              *reinterpret_cast<const uint4*>(stg + row * (D * 2) + ((c ^ (row % kChunks)) << 4));
+          reinterpret_cast<uint4*>(orow)[c] = *reinterpret_cast<const uint4*>(
+              stg + (c >> 3) * S::kQRegionBytes + tc::sw128_offset(row, c & 7));
         }
       }
     }
@@ -629,7 +653,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
 template <typename E, int D>
 int launch_tc_t(const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensorMap& qmap,
-                const PrefillParams& p, dim3 grid, cudaStream_t stream) {
+                const CUtensorMap& omap, const PrefillParams& p, dim3 grid, cudaStream_t stream) {
   // Over half of the SM's shared memory, so one CTA (512 TMEM columns) per SM.
   const int smem = std::max(fa_smem_layout<D>().total + 1024, 116 * 1024);
   auto kern = paged_prefill_tc_kernel<E, D>;
@@ -651,7 +675,7 @@ int launch_tc_t(const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensor
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t lerr = cudaLaunchKernelEx(&cfg, kern, kmap, vmap, qmap, p);
+  const cudaError_t lerr = cudaLaunchKernelEx(&cfg, kern, kmap, vmap, qmap, omap, p);
   if (lerr != cudaSuccess) return cuda_status(lerr, "paged_prefill_tc_kernel launch");
   return cuda_status(cudaGetLastError(), "paged_prefill_tc_kernel launch");
 }
@@ -663,15 +687,15 @@ int prefill_tc_query_block(int group) { return fa_query_block(group); }
 int prefill_tc_query_heads_per_tile(int group) { return group >= 2 ? group / 2 : 1; }
 
 int launch_prefill_tc(const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensorMap& qmap,
-                      const PrefillParams& p, int head_dim, bool bf16, unsigned grid_x,
-                      unsigned grid_y, cudaStream_t stream) {
+                      const CUtensorMap& omap, const PrefillParams& p, int head_dim, bool bf16,
+                      unsigned grid_x, unsigned grid_y, cudaStream_t stream) {
   const dim3 grid(grid_x, grid_y);
   if (head_dim == 128)
-    return bf16 ? launch_tc_t<BF16, 128>(kmap, vmap, qmap, p, grid, stream)
-                : launch_tc_t<Half, 128>(kmap, vmap, qmap, p, grid, stream);
+    return bf16 ? launch_tc_t<BF16, 128>(kmap, vmap, qmap, omap, p, grid, stream)
+                : launch_tc_t<Half, 128>(kmap, vmap, qmap, omap, p, grid, stream);
   if (head_dim == 64)
-    return bf16 ? launch_tc_t<BF16, 64>(kmap, vmap, qmap, p, grid, stream)
-                : launch_tc_t<Half, 64>(kmap, vmap, qmap, p, grid, stream);
+    return bf16 ? launch_tc_t<BF16, 64>(kmap, vmap, qmap, omap, p, grid, stream)
+                : launch_tc_t<Half, 64>(kmap, vmap, qmap, omap, p, grid, stream);
   return set_error(B200_ERR_UNSUPPORTED, "tcgen05 prefill supports head_dim 64 and 128");
 }
 
