@@ -8,6 +8,8 @@
 // bit-exact by construction (the reference's own test is torch.equal,
 // tests/test_attention.py:196-207).  When a source row is not 16-byte aligned
 // the kernel falls back to 2-byte elements (same result, slower).
+#include <algorithm>
+
 #include "../../include/b200_paged_attn.h"
 #include "append.h"
 #include "common.cuh"
@@ -32,6 +34,9 @@ struct AppendParams {
   int slots64;
 };
 
+// One CTA per token: its threads walk the token's num_kv_heads x row vectors.
+// The token's slot is read once per thread (one broadcast transaction) and the
+// K/V loads are issued without waiting for it; index math is 32-bit.
 template <typename V>
 __global__ void __launch_bounds__(256) append_kv_kernel(const AppendParams p) {
   // Launched with programmatic stream serialization: no global access before
@@ -39,26 +44,21 @@ __global__ void __launch_bounds__(256) append_kv_kernel(const AppendParams p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int vec_per_row = p.row_bytes / static_cast<int>(sizeof(V));
-  const long long per_token = static_cast<long long>(p.num_kv_heads) * vec_per_row;
-  const long long total = p.num_tokens * per_token;
-  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long t = idx / per_token;
-    const int rem = static_cast<int>(idx - t * per_token);
-    const int h = rem / vec_per_row;
-    const int v = rem - h * vec_per_row;
-    const long long slot = load_index(p.slots, t, p.slots64);
-    if (slot < 0) continue;  // padding slot
-    if (slot >= p.num_slots) {
-      if (p.err) atomicOr(p.err, kErrBadSlot);
-      continue;
-    }
+  const int items = p.num_kv_heads * vec_per_row;
+  const long long t = blockIdx.x;
+  const long long slot = load_index(p.slots, t, p.slots64);
+  if (slot >= p.num_slots && threadIdx.x == 0 && p.err) atomicOr(p.err, kErrBadSlot);
+  const bool slot_ok = slot >= 0 && slot < p.num_slots;  // negative: padding, skipped
+  const uint8_t* key = p.key + t * p.key_stride_token;
+  const uint8_t* value = p.value + t * p.value_stride_token;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int h = it / vec_per_row;
+    const int v = it - h * vec_per_row;
+    const V kv = *reinterpret_cast<const V*>(key + h * p.key_stride_head + v * sizeof(V));
+    const V vv = *reinterpret_cast<const V*>(value + h * p.value_stride_head + v * sizeof(V));
+    if (!slot_ok) continue;
     const long long dst =
         ((p.layer_slot_base + slot) * p.num_kv_heads + h) * p.row_bytes + v * sizeof(V);
-    const V kv = *reinterpret_cast<const V*>(p.key + t * p.key_stride_token +
-                                             h * p.key_stride_head + v * sizeof(V));
-    const V vv = *reinterpret_cast<const V*>(p.value + t * p.value_stride_token +
-                                             h * p.value_stride_head + v * sizeof(V));
     *reinterpret_cast<V*>(p.k_cache + dst) = kv;
     *reinterpret_cast<V*>(p.v_cache + dst) = vv;
   }
@@ -104,15 +104,16 @@ int launch_append_kv(const b200_cache_desc* c, int32_t layer, const void* key, c
                                                  p.row_bytes);
   const bool vec16 = (align & 15) == 0;
   const long long vec_per_row = vec16 ? p.row_bytes / 16 : p.row_bytes / 2;
-  const long long total = num_tokens * c->num_kv_heads * vec_per_row;
-  const int threads = 256;
-  long long blocks = (total + threads - 1) / threads;
-  if (blocks > 148LL * 64) blocks = 148LL * 64;
+  // One CTA per token, as many threads as its vectors (a multiple of 32, <= 256).
+  if (num_tokens > 0x7fffffffLL)
+    return set_error(B200_ERR_UNSUPPORTED, "append is limited to 2^31 - 1 tokens");
+  const long long items = c->num_kv_heads * vec_per_row;
+  if (items > 0x7fffffffLL) return set_error(B200_ERR_UNSUPPORTED, "too many kv heads");
+  const int threads = static_cast<int>(std::min<long long>(256, (items + 31) / 32 * 32));
+  const dim3 grid(static_cast<unsigned>(num_tokens));
   const cudaError_t err =
-      vec16 ? launch_dependent(append_kv_kernel<uint4>, dim3(static_cast<unsigned>(blocks)),
-                               dim3(threads), 0, stream, p)
-            : launch_dependent(append_kv_kernel<uint16_t>, dim3(static_cast<unsigned>(blocks)),
-                               dim3(threads), 0, stream, p);
+      vec16 ? launch_dependent(append_kv_kernel<uint4>, grid, dim3(threads), 0, stream, p)
+            : launch_dependent(append_kv_kernel<uint16_t>, grid, dim3(threads), 0, stream, p);
   return cuda_status(err, "append_kv_kernel launch");
 }
 

@@ -12,6 +12,8 @@
 // (x*cos, rotate_half(x)*sin, their sum): its output is bit-identical to the
 // reference's, and the appended K/V equal what append_kv would store.
 // One launch replaces the rotary ops, the layout copies and the append.
+#include <algorithm>
+
 #include "../../include/b200_paged_attn.h"
 #include "common.cuh"
 #include "host_common.h"
@@ -56,34 +58,31 @@ __device__ __forceinline__ void lane_set(Vec8& v, int i, float x) {
   memcpy(&v.h[i], &t, 2);
 }
 
-// One work item = W consecutive pair indices i..i+W-1 of one row (W = 8 with
-// 16-byte vectors, else 1).  Rows per token: q heads, then k heads (rotated),
-// then v heads (copied).
+// One CTA per token; its threads walk the token's work items: W consecutive
+// pair indices i..i+W-1 of one row (W = 8 with 16-byte vectors, else 1).  Rows:
+// q heads, then k heads (rotated), then v heads (copied).  All index math is
+// 32-bit within a token; the token's slot is read once per thread (one
+// broadcast transaction) and every load of an item is issued before the slot
+// is checked, so loads are not queued behind the slot's round trip.
 template <typename E, int W>
-__global__ void __launch_bounds__(256) rope_append_kernel(const RopeParams p) {
+__global__ void __launch_bounds__(1024) rope_append_kernel(const RopeParams p) {
   using T = typename E::T;
   const int half = p.head_dim / 2;
   const int items_per_row = half / W;
   const int rot_rows = p.num_q_heads + p.num_kv_heads;
-  const long long per_token = static_cast<long long>(rot_rows + p.num_kv_heads) * items_per_row;
-  const long long total = p.num_tokens * per_token;
-  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long t = idx / per_token;
-    const int rem = static_cast<int>(idx - t * per_token);
-    const int row = rem / items_per_row;
-    const int i = (rem - row * items_per_row) * W;
+  const int items = (rot_rows + p.num_kv_heads) * items_per_row;
+  const long long t = blockIdx.x;
+  const long long slot = load_index(p.slots, t, p.slots64);
+  const bool slot_ok = slot >= 0 && slot < p.num_slots;
+  if (slot >= p.num_slots && threadIdx.x == 0 && p.err) atomicOr(p.err, kErrBadSlot);
+  const T* c = reinterpret_cast<const T*>(p.cos) + t * p.cos_st;
+  const T* s = reinterpret_cast<const T*>(p.sin) + t * p.sin_st;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int row = it / items_per_row;
+    const int i = (it - row * items_per_row) * W;
     const bool is_q = row < p.num_q_heads;
     const bool is_k = !is_q && row < rot_rows;
-    long long slot = 0;
-    if (!is_q) {
-      slot = load_index(p.slots, t, p.slots64);
-      if (slot < 0) continue;  // padding slot: nothing to append
-      if (slot >= p.num_slots) {
-        if (p.err) atomicOr(p.err, kErrBadSlot);
-        continue;
-      }
-    }
+    if (!is_q && !slot_ok) continue;  // padding (negative) or out-of-pool slot: no append
     const T* src;
     T* dst;
     if (is_q) {
@@ -108,8 +107,6 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeParams p) {
         *reinterpret_cast<Vec8*>(dst + i + half) = x2;
         continue;
       }
-      const T* c = reinterpret_cast<const T*>(p.cos) + t * p.cos_st;
-      const T* s = reinterpret_cast<const T*>(p.sin) + t * p.sin_st;
       const Vec8 c1 = *reinterpret_cast<const Vec8*>(c + i);
       const Vec8 c2 = *reinterpret_cast<const Vec8*>(c + i + half);
       const Vec8 s1 = *reinterpret_cast<const Vec8*>(s + i);
@@ -132,8 +129,6 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeParams p) {
         dst[i + half] = src[i + half];
         continue;
       }
-      const T* c = reinterpret_cast<const T*>(p.cos) + t * p.cos_st;
-      const T* s = reinterpret_cast<const T*>(p.sin) + t * p.sin_st;
       float l, h;
       rope_pair<E>(to_float<E>(src[i]), to_float<E>(src[i + half]), to_float<E>(c[i]),
                    to_float<E>(s[i]), to_float<E>(c[i + half]), to_float<E>(s[i + half]), l, h);
@@ -201,21 +196,25 @@ int launch_rope_append(const b200_cache_desc* c, const b200_rope_append_args* a,
                    aligned16(cos) && aligned16(sin) && aligned16(query_out) &&
                    aligned16(c->k_cache) && aligned16(c->v_cache);
   const int width = vec ? 8 : 1;
-  const long long work =
-      a->num_tokens * (a->num_q_heads + 2LL * c->num_kv_heads) * (c->head_dim / 2 / width);
-  long long blocks = (work + 255) / 256;
-  if (blocks > 148LL * 32) blocks = 148LL * 32;
-  const unsigned b = static_cast<unsigned>(blocks);
+  // One CTA per token: its (Hq + 2 Hkv) x head_dim / (2 width) items.
+  if (a->num_tokens > 0x7fffffffLL)
+    return set_error(B200_ERR_UNSUPPORTED, "rotary append is limited to 2^31 - 1 tokens");
+  const long long items =
+      (a->num_q_heads + 2LL * c->num_kv_heads) * (c->head_dim / 2 / width);
+  if (items > 0x7fffffffLL) return set_error(B200_ERR_UNSUPPORTED, "too many heads per token");
+  const unsigned b = static_cast<unsigned>(a->num_tokens);
+  // A thread per item (up to 1024): every load of a token is in flight at once.
+  const unsigned t = static_cast<unsigned>(std::min<long long>(1024, (items + 31) / 32 * 32));
   if (c->dtype == B200_BF16) {
     if (vec)
-      rope_append_kernel<BF16, 8><<<b, 256, 0, stream>>>(p);
+      rope_append_kernel<BF16, 8><<<b, t, 0, stream>>>(p);
     else
-      rope_append_kernel<BF16, 1><<<b, 256, 0, stream>>>(p);
+      rope_append_kernel<BF16, 1><<<b, t, 0, stream>>>(p);
   } else {
     if (vec)
-      rope_append_kernel<Half, 8><<<b, 256, 0, stream>>>(p);
+      rope_append_kernel<Half, 8><<<b, t, 0, stream>>>(p);
     else
-      rope_append_kernel<Half, 1><<<b, 256, 0, stream>>>(p);
+      rope_append_kernel<Half, 1><<<b, t, 0, stream>>>(p);
   }
   return cuda_status(cudaGetLastError(), "rope_append_kernel launch");
 }
