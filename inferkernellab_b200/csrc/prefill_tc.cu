@@ -50,7 +50,9 @@
 #include "tcgen05.cuh"
 
 namespace b200 {
+
 namespace {
+
 constexpr int kFaTiles = 2;                       // query tiles per CTA
 constexpr int kFaKeys = 2 * kKvTile;              // keys per K/V stage
 constexpr int kFaProducerWarp = 8;

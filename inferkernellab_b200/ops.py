@@ -558,13 +558,23 @@ def _prefill_kernel(kernel: str) -> int:
 
 
 def paged_prefill_attention(query: torch.Tensor, cache, block_tables, query_starts, context_lens,
-                            *, scale=None, layer: int = 0, kernel: str = "auto") -> torch.Tensor:
+                            *, scale=None, layer: int = 0, kernel: str = "auto",
+                            validate_inputs: bool = True) -> torch.Tensor:
     """Ragged causal prefill over the paged cache, padded ``[B, Hq, T, D]`` form.
 
     Drop-in for ``paged_prefill_attention_sdpa`` (reference ``attention.py:230-321``):
     row ``b`` holds query positions ``query_starts[b] .. context_lens[b]-1``;
     padded rows attend key 0 only, as in the reference mask.  The cache must
     already hold every key of each range.
+
+    ``validate_inputs=True`` (the reference's behaviour) reads the ranges to the
+    host -- a synchronisation when they are device tensors -- and raises the
+    reference's ``ValueError`` for an empty or negative range, a range wider
+    than the query or a context past the block table.  ``False`` skips those
+    checks and passes device tensors straight to the kernel with no host
+    synchronisation (an invalid range is then computed as an empty one, its rows
+    attending key 0 like padding rows, and a context past the block table is cut
+    at the table's end).
     """
     if query.ndim != 4:
         raise ValueError("query must be [B,H,T,D]")
@@ -576,15 +586,6 @@ def paged_prefill_attention(query: torch.Tensor, cache, block_tables, query_star
         raise ValueError("num_heads must be divisible by num_kv_heads")
     if query.device != cache.k.device or query.device.type != "cuda":
         raise ValueError("query and cache must be on the same device")
-    starts_t, starts = _prefill_index(query_starts, query.device)
-    ends_t, ends = _prefill_index(context_lens, query.device)
-    if len(starts) != batch or len(ends) != batch:
-        raise ValueError("query_starts and context_lens must have one entry per query batch")
-    lengths = [e - s for s, e in zip(starts, ends)]
-    if any(s < 0 or n <= 0 for s, n in zip(starts, lengths)):
-        raise ValueError("prefill ranges must be non-empty and non-negative")
-    if max(lengths) > query_width:
-        raise ValueError("query width is smaller than a prefill range")
     if not 0 <= layer < layout.num_layers:
         raise IndexError("layer is out of range")
     if isinstance(block_tables, torch.Tensor):
@@ -595,8 +596,25 @@ def paged_prefill_attention(query: torch.Tensor, cache, block_tables, query_star
         raise ValueError("block_tables must have one row per query batch")
     if tables.dtype not in _INDEX_CODE:
         tables = tables.to(torch.int64)
-    if -(-max(ends) // layout.block_size) > tables.shape[1]:
-        raise ValueError("context length exceeds block table capacity")
+    device_ranges = (not validate_inputs and isinstance(query_starts, torch.Tensor)
+                     and isinstance(context_lens, torch.Tensor))
+    if device_ranges:
+        starts_t = query_starts.to(device=query.device, dtype=torch.int64)
+        ends_t = context_lens.to(device=query.device, dtype=torch.int64)
+        if starts_t.shape != (batch,) or ends_t.shape != (batch,):
+            raise ValueError("query_starts and context_lens must have one entry per query batch")
+    else:
+        starts_t, starts = _prefill_index(query_starts, query.device)
+        ends_t, ends = _prefill_index(context_lens, query.device)
+        if len(starts) != batch or len(ends) != batch:
+            raise ValueError("query_starts and context_lens must have one entry per query batch")
+        lengths = [e - s for s, e in zip(starts, ends)]
+        if any(s < 0 or n <= 0 for s, n in zip(starts, lengths)):
+            raise ValueError("prefill ranges must be non-empty and non-negative")
+        if max(lengths) > query_width:
+            raise ValueError("query width is smaller than a prefill range")
+        if -(-max(ends) // layout.block_size) > tables.shape[1]:
+            raise ValueError("context length exceeds block table capacity")
     if query.dtype != cache.k.dtype:
         raise ValueError("query and cache must have the same dtype")
     if query.stride(-1) != 1 or query.stride(0) % 2 or query.stride(1) % 2 or query.stride(2) % 2:
@@ -612,7 +630,7 @@ def paged_prefill_attention(query: torch.Tensor, cache, block_tables, query_star
         float(scale) if scale is not None else head_dim ** -0.5, _prefill_kernel(kernel))
     _lib.check(_lib.load().b200_paged_prefill(
         ctypes.byref(desc), ctypes.byref(args), query.data_ptr(), tables.data_ptr(),
-        starts_t.data_ptr(), ends_t.data_ptr(), None, out.data_ptr(),
+        starts_t.contiguous().data_ptr(), ends_t.contiguous().data_ptr(), None, out.data_ptr(),
         _ERROR_WORDS.get(query.device).data_ptr(), _stream_ptr(query.device)))
     return out
 

@@ -181,6 +181,27 @@ def test_prefill_varlen_matches_padded_and_skips_nan_slots():
     assert_close(padded, want, dtype, "varlen nan")
 
 
+@pytest.mark.parametrize("kernel", ["tcgen05", "mma_sync"])
+def test_prefill_padded_without_validation_never_synchronises(kernel):
+    """validate_inputs=False with device ranges: no host synchronisation (torch's
+    sync debug mode raises on one) and the same output as the validating call."""
+    dtype = torch.bfloat16
+    starts, ends = [0, 33, 7], [97, 50, 8]
+    cache, tables, query = _prefill_case(dtype, 16, 4, 64, 16, starts, ends, seed=5)
+    want = paged_prefill_attention(query, cache, tables, starts, ends, kernel=kernel)
+    tables_d = torch.tensor(tables, dtype=torch.int32, device="cuda")
+    starts_d = torch.tensor(starts, dtype=torch.int32, device="cuda")
+    ends_d = torch.tensor(ends, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        out = paged_prefill_attention(query, cache, tables_d, starts_d, ends_d, kernel=kernel,
+                                      validate_inputs=False)
+    finally:
+        torch.cuda.set_sync_debug_mode("default")
+    assert torch.equal(out, want)
+
+
 def test_prefill_rejects_bad_ranges():
     cache = PagedKVCache(8, 4, 2, 16, dtype=torch.float16, device="cuda")
     query = torch.randn(1, 4, 4, 16, dtype=torch.float16, device="cuda")
