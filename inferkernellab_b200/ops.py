@@ -174,6 +174,21 @@ def _as_index_tensor(values, device: torch.device) -> torch.Tensor:
     return values
 
 
+def _as_table_tensor(tables, device: torch.device) -> torch.Tensor:
+    """Block tables as a 2-D index tensor; ragged Python rows are padded with 0.
+
+    The reference's ``paged_reference`` backend passes one Python list per
+    request (``decode.py:400-402``), of different lengths; the Triton backends
+    pass a padded ``[B, W]`` tensor.  Entries past a row's context are never
+    read, so padding them with block 0 changes nothing.
+    """
+    if isinstance(tables, (list, tuple)) and tables and all(
+            isinstance(row, (list, tuple)) for row in tables):
+        width = max(len(row) for row in tables)
+        tables = [list(row) + [0] * (width - len(row)) for row in tables]
+    return _as_index_tensor(list(tables) if isinstance(tables, tuple) else tables, device)
+
+
 def paged_decode_attention(query: torch.Tensor, cache, block_tables, context_lens, scale=None,
                            layer: int = 0, *, validate_inputs: bool = True,
                            out: torch.Tensor | None = None) -> torch.Tensor:
@@ -191,7 +206,7 @@ def paged_decode_attention(query: torch.Tensor, cache, block_tables, context_len
         raise ValueError("query dimensions must be positive")
     if query.stride(-1) != 1:
         raise ValueError("query must be contiguous in the head_dim dimension")
-    block_tables = _as_index_tensor(block_tables, query.device)
+    block_tables = _as_table_tensor(block_tables, query.device)
     context_lens = _as_index_tensor(context_lens, query.device)
     layout = cache.layout
     if not 0 <= layer < layout.num_layers:
@@ -311,7 +326,7 @@ def paged_decode_attention_append(query: torch.Tensor, key: torch.Tensor, value:
         cos, sin = (t if _rows16(t) else t.contiguous() for t in (cos, sin))
     if slots.numel() != batch or slots.dtype not in _INDEX_CODE or slots.device != device:
         raise ValueError("slots must be one int32/int64 entry per request on the query device")
-    block_tables = _as_index_tensor(block_tables, device)
+    block_tables = _as_table_tensor(block_tables, device)
     context_lens = _as_index_tensor(context_lens, device)
     if block_tables.ndim != 2 or block_tables.shape[0] != batch:
         raise ValueError("block_tables must have shape [B, max_blocks]")
@@ -591,7 +606,7 @@ def paged_prefill_attention(query: torch.Tensor, cache, block_tables, query_star
     if isinstance(block_tables, torch.Tensor):
         tables = block_tables.to(device=query.device)
     else:
-        tables = torch.as_tensor(block_tables, dtype=torch.int64, device=query.device)
+        tables = _as_table_tensor(block_tables, query.device)
     if tables.ndim != 2 or tables.shape[0] != batch:
         raise ValueError("block_tables must have one row per query batch")
     if tables.dtype not in _INDEX_CODE:

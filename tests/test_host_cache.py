@@ -77,3 +77,16 @@ def test_cache_validation_and_layout():
     assert tuple(cache.k.shape) == (3, 5, 8, 2, 32)
     assert cache.numel_bytes == 2 * 3 * 5 * 8 * 2 * 32 * 2
     assert cache.dtype == torch.bfloat16
+
+
+def test_ragged_list_tables_pad_with_block_zero():
+    # The reference's paged_reference backend hands the operators one Python
+    # list per request; rows past a request's context are never read.
+    from inferkernellab_b200.ops import _as_table_tensor
+
+    cpu = torch.device("cpu")
+    t = _as_table_tensor([[3, 1, 4], [1], (5, 9)], cpu)
+    assert t.dtype == torch.int32 and t.tolist() == [[3, 1, 4], [1, 0, 0], [5, 9, 0]]
+    assert _as_table_tensor([[2, 7], [1, 8]], cpu).tolist() == [[2, 7], [1, 8]]
+    dev = torch.zeros(2, 3, dtype=torch.int64)
+    assert _as_table_tensor(dev, cpu) is dev
