@@ -629,6 +629,26 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   uint32_t qb[NT][D / 16][2];
   float oT[NT][D / 16][4];
   float m_t[NT][2], l_t[NT][2];
+  // Running softmax state to its empty value.  Done at the start and again as
+  // soon as a segment's state has been handed to shared memory, so that it holds
+  // constants (no live registers) through the publish and merge that follow.
+  auto reset_state = [&]() {
+    if constexpr (kTrans) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int i = 0; i < D / 16; ++i) oT[nt][i][0] = oT[nt][i][1] = oT[nt][i][2] = oT[nt][i][3] = 0.f;
+        m_t[nt][0] = m_t[nt][1] = -INFINITY;
+        l_t[nt][0] = l_t[nt][1] = 0.f;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      m_r[0] = m_r[1] = -INFINITY;
+      l_r[0] = l_r[1] = 0.f;
+    }
+  };
+  reset_state();
   bool aborted = false;
 
   TileCursor cur;
@@ -648,20 +668,9 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       const long long q_head_stride = staged ? p.out_stride_head : p.q_stride_head;
       if constexpr (kTrans) {
         load_qT_frag<E, D, NT>(qb, qg, q_head_stride, G, lane);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-          for (int i = 0; i < D / 16; ++i) oT[nt][i][0] = oT[nt][i][1] = oT[nt][i][2] = oT[nt][i][3] = 0.f;
-          m_t[nt][0] = m_t[nt][1] = -INFINITY;
-          l_t[nt][0] = l_t[nt][1] = 0.f;
-        }
       } else {
         load_q_frag<E, D>(qf, row0 < G ? qg + row0 * q_head_stride : nullptr,
                           row1 < G ? qg + row1 * q_head_stride : nullptr, tq);
-#pragma unroll
-        for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-        m_r[0] = m_r[1] = -INFINITY;
-        l_r[0] = l_r[1] = 0.f;
       }
     }
 
@@ -773,6 +782,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
           }
         }
       }
+      reset_state();
       named_bar_sync(1, kConsumers);
       // Per-row slice weights, once per row (segment rows = the GH query heads).
       if (!aborted) {
@@ -846,103 +856,127 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
             const int q = p_first + i;
             return seg_begin <= q * per_cta ? 2 * q : 2 * q + 1;
           };
-          // One pass over the pieces' lse: running max and rescaled sum per lane,
-          // then combined across the warp.  With few pieces the lse values stay
-          // in merge_w for the weights below (no second global read).
-          const bool lse_cached = npieces <= kMergeChunk;
-          for (int row = warp; row < GH; row += kDecConsumerWarps) {
-            float m = -INFINITY, sum = 0.f;
-            for (int i = lane; i < npieces; i += 32) {
-              const float lse = __ldcg(p.part_lse + piece_slot(i) * GH + row);
-              if (lse_cached) merge_w[i * GH + row] = lse;
-              if (lse == -INFINITY) continue;
-              if (lse > m) {
-                sum = (m == -INFINITY ? 0.f : sum * fast_exp2(m - lse)) + 1.f;
-                m = lse;
-              } else {
-                sum += fast_exp2(lse - m);
-              }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-              const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-              const float s2 = __shfl_xor_sync(0xffffffffu, sum, o);
-              const float mm = fmaxf(m, m2);
-              if (mm != -INFINITY) {
-                sum = (m == -INFINITY ? 0.f : sum * fast_exp2(m - mm)) +
-                      (m2 == -INFINITY ? 0.f : s2 * fast_exp2(m2 - mm));
-                m = mm;
-              }
-            }
-            if (lane == 0) {
-              row_base[row] = m == -INFINITY ? 0.f : m;
-              row_l[row] = 1.f / sum;
-            }
-          }
-          named_bar_sync(1, kConsumers);
           float4 acc[kElems4];
 #pragma unroll
           for (int k4 = 0; k4 < kElems4; ++k4) acc[k4] = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int c0 = 0; c0 < npieces; c0 += kMergeChunk) {
-            const int nq = min(kMergeChunk, npieces - c0);
-            for (int i = tid; i < kMergeChunk * GH; i += kConsumers) {
-              const int q = i / GH;
-              const int row = i - q * GH;
-              float w = 0.f;
-              if (q < nq) {
-                const float lse =
-                    lse_cached ? merge_w[i] : __ldcg(p.part_lse + piece_slot(c0 + q) * GH + row);
-                if (lse != -INFINITY) w = fast_exp2(lse - row_base[row]) * row_l[row];
+          if constexpr (kTrans) {
+            // One pass, no shared memory.  Thread t owns the kElems4 consecutive
+            // outputs t * kElems4 ..: one row, so one lse and one running max /
+            // rescaled sum per piece.  Each batch loads the lse and the partial O
+            // of kPB pieces (16 float4 plus kPB lse, all independent), then folds
+            // them in piece order, so a merge of n pieces costs about n / kPB L2
+            // round trips in all.  Pieces without a visible key (lse = -inf;
+            // their partial is 0/0) are skipped.
+            static_assert(kD4 % kElems4 == 0, "a thread's merge outputs share one row");
+            constexpr int kPB = 16 / kElems4;
+            const int e0 = tid * kElems4;
+            const int row = e0 / kD4;
+            const int d40 = e0 - row * kD4;
+            const bool mine = e0 < GH * kD4;
+            float m_run = -INFINITY, s_run = 0.f;
+            for (int q0 = 0; q0 < npieces; q0 += kPB) {
+              float lse[kPB];
+              float4 v[kPB][kElems4];
+#pragma unroll
+              for (int u = 0; u < kPB; ++u) {
+                const bool in = mine && q0 + u < npieces;
+                const long long base = in ? static_cast<long long>(piece_slot(q0 + u)) * GH + row : 0;
+                lse[u] = in ? __ldcg(p.part_lse + base) : -INFINITY;
+#pragma unroll
+                for (int j = 0; j < kElems4; ++j)
+                  v[u][j] = in ? __ldcg(reinterpret_cast<const float4*>(p.part_o) + base * kD4 +
+                                        d40 + j)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
               }
-              merge_w[i] = w;
-            }
-            named_bar_sync(1, kConsumers);
-            if constexpr (kTrans) {
-              // Pieces in batches for (at most) 4 outputs of this thread: every
-              // load of a batch (16 float4: 4 pieces x 4 outputs at head_dim 128,
-              // 8 x 2 at 64, 16 x 1 below) is issued before any is used, so a
-              // merge of n pieces costs about n / kPB L2 round trips.  Pieces
-              // with zero weight (no visible key: their partial is 0/0) are
-              // neither loaded nor added.
-              constexpr int kGrp = kElems4 < 4 ? kElems4 : 4;
-              constexpr int kPB = 16 / kGrp;
 #pragma unroll
-              for (int g0 = 0; g0 < kElems4; g0 += kGrp) {
-                for (int q0 = 0; q0 < nq; q0 += kPB) {
-                  float w[kPB][kGrp];
-                  float4 v[kPB][kGrp];
+              for (int u = 0; u < kPB; ++u) {
+                const float l = lse[u];
+                if (l == -INFINITY) continue;
+                float c = 1.f, w = 1.f;
+                if (l > m_run) {
+                  c = m_run == -INFINITY ? 0.f : fast_exp2(m_run - l);
+                  m_run = l;
+                } else {
+                  w = fast_exp2(l - m_run);
+                }
+                s_run = s_run * c + w;
 #pragma unroll
-                  for (int u = 0; u < kPB; ++u) {
-                    const int q = q0 + u;
-                    const bool have = q < nq;
-                    const long long slot_q = have ? piece_slot(c0 + q) : 0;
-#pragma unroll
-                    for (int j = 0; j < kGrp; ++j) {
-                      const int e = tid + (g0 + j) * kConsumers;
-                      const int row = e / kD4;
-                      const int d4 = e - row * kD4;
-                      const bool in = have && e < GH * kD4;
-                      w[u][j] = in ? merge_w[q * GH + row] : 0.f;
-                      v[u][j] = w[u][j] != 0.f
-                                    ? __ldcg(reinterpret_cast<const float4*>(p.part_o) +
-                                             (slot_q * GH + row) * kD4 + d4)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-                  }
-#pragma unroll
-                  for (int u = 0; u < kPB; ++u)
-#pragma unroll
-                    for (int j = 0; j < kGrp; ++j) {
-                      acc[g0 + j].x += w[u][j] * v[u][j].x;
-                      acc[g0 + j].y += w[u][j] * v[u][j].y;
-                      acc[g0 + j].z += w[u][j] * v[u][j].z;
-                      acc[g0 + j].w += w[u][j] * v[u][j].w;
-                    }
+                for (int j = 0; j < kElems4; ++j) {
+                  acc[j].x = acc[j].x * c + w * v[u][j].x;
+                  acc[j].y = acc[j].y * c + w * v[u][j].y;
+                  acc[j].z = acc[j].z * c + w * v[u][j].z;
+                  acc[j].w = acc[j].w * c + w * v[u][j].w;
                 }
               }
-            } else {
-              // Heads-as-M (G > 16): its main-loop state leaves no registers for
-              // batches; one piece at a time.
+            }
+            // No visible key in any piece: 0, the weighted sum of no pieces.
+            const float inv = s_run > 0.f ? 1.f / s_run : 0.f;
+            if (mine) {
+#pragma unroll
+              for (int j = 0; j < kElems4; ++j) {
+                acc[j].x *= inv;
+                acc[j].y *= inv;
+                acc[j].z *= inv;
+                acc[j].w *= inv;
+                store4<E>(out_seg + row * p.out_stride_head + (d40 + j) * 4, acc[j]);
+              }
+            }
+          } else {
+            // Heads-as-M (G > 16): its main-loop state leaves no registers for
+            // batches of O.  The lse of every (piece, row) of a chunk is loaded
+            // at once (independent loads) into merge_w, then each row folds its
+            // pieces in order into a running max and rescaled sum.  With few
+            // pieces the lse values stay in merge_w for the weights below (no
+            // second global read).
+            const bool lse_cached = npieces <= kMergeChunk;
+            for (int row = tid; row < GH; row += kConsumers) {
+              row_base[row] = -INFINITY;
+              row_l[row] = 0.f;
+            }
+            for (int c0 = 0; c0 < npieces; c0 += kMergeChunk) {
+              const int nq = min(kMergeChunk, npieces - c0);
+#pragma unroll 4
+              for (int i = tid; i < nq * GH; i += kConsumers) {
+                const int q = i / GH;
+                merge_w[i] = __ldcg(p.part_lse + piece_slot(c0 + q) * GH + (i - q * GH));
+              }
+              named_bar_sync(1, kConsumers);
+              for (int row = tid; row < GH; row += kConsumers) {
+                float m = row_base[row], sum = row_l[row];
+                for (int q = 0; q < nq; ++q) {
+                  const float lse = merge_w[q * GH + row];
+                  if (lse == -INFINITY) continue;
+                  if (lse > m) {
+                    sum = (m == -INFINITY ? 0.f : sum * fast_exp2(m - lse)) + 1.f;
+                    m = lse;
+                  } else {
+                    sum += fast_exp2(lse - m);
+                  }
+                }
+                row_base[row] = m;
+                row_l[row] = sum;
+              }
+              named_bar_sync(1, kConsumers);
+            }
+            for (int row = tid; row < GH; row += kConsumers) {
+              row_base[row] = row_base[row] == -INFINITY ? 0.f : row_base[row];
+              row_l[row] = 1.f / row_l[row];
+            }
+            named_bar_sync(1, kConsumers);
+            for (int c0 = 0; c0 < npieces; c0 += kMergeChunk) {
+              const int nq = min(kMergeChunk, npieces - c0);
+              for (int i = tid; i < kMergeChunk * GH; i += kConsumers) {
+                const int q = i / GH;
+                const int row = i - q * GH;
+                float w = 0.f;
+                if (q < nq) {
+                  const float lse =
+                      lse_cached ? merge_w[i] : __ldcg(p.part_lse + piece_slot(c0 + q) * GH + row);
+                  if (lse != -INFINITY) w = fast_exp2(lse - row_base[row]) * row_l[row];
+                }
+                merge_w[i] = w;
+              }
+              named_bar_sync(1, kConsumers);
 #pragma unroll
               for (int k4 = 0; k4 < kElems4; ++k4) {
                 const int e = tid + k4 * kConsumers;
@@ -963,15 +997,15 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
                   }
                 }
               }
+              named_bar_sync(1, kConsumers);
             }
-            named_bar_sync(1, kConsumers);
-          }
 #pragma unroll
-          for (int k4 = 0; k4 < kElems4; ++k4) {
-            const int e = tid + k4 * kConsumers;
-            if (e < GH * kD4) {
-              const int row = e / kD4;
-              store4<E>(out_seg + row * p.out_stride_head + (e - row * kD4) * 4, acc[k4]);
+            for (int k4 = 0; k4 < kElems4; ++k4) {
+              const int e = tid + k4 * kConsumers;
+              if (e < GH * kD4) {
+                const int row = e / kD4;
+                store4<E>(out_seg + row * p.out_stride_head + (e - row * kD4) * 4, acc[k4]);
+              }
             }
           }
           if (tid == 0) p.counters[seg] = 0;
