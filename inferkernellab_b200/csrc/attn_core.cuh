@@ -54,27 +54,45 @@ struct TableWindow {
   int count;  // pages held
 };
 
+// kWide: a window of more than 128 pages is loaded with every load issued
+// before any is stored -- one L2/HBM round trip, not one per 128 pages -- at the
+// cost of 16 live registers per lane and a longer code path; shorter windows
+// always take the 128-page loop.  Decode asks for it (its long rows wait on this
+// refill before their first TMA); the prefill kernels do not.
+template <bool kWide = false>
 __device__ __forceinline__ void table_window_refill(TableWindow& w, const PagedSource& src,
                                                     int row, int first_page, int row_pages,
                                                     uint32_t* err, int lane) {
   const int count = min(kTableWindow, row_pages - first_page);
   const long long base = static_cast<long long>(row) * src.table_stride + first_page;
+  auto put = [&](int i, long long v) {
+    const bool ok = v >= 0 && v < src.num_blocks;
+    if (!ok && err) atomicOr(err, kErrBadBlock);
+    w.ids[i] = ok ? static_cast<int>(v) : -1;
+  };
   __syncwarp();
-  for (int i0 = 0; i0 < count; i0 += 128) {
-    long long v[4];
+  if (kWide && count > 128) {
+    constexpr int kPer = kTableWindow / 32;
+    long long v[kPer];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u * 32 + lane;
+    for (int u = 0; u < kPer; ++u) {
+      const int i = u * 32 + lane;
       v[u] = i < count ? load_index(src.tables, base + i, src.table64) : 0;
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u * 32 + lane;
-      if (i < count) {
-        const bool ok = v[u] >= 0 && v[u] < src.num_blocks;
-        if (!ok && err) atomicOr(err, kErrBadBlock);
-        w.ids[i] = ok ? static_cast<int>(v[u]) : -1;
+    for (int u = 0; u < kPer; ++u)
+      if (u * 32 + lane < count) put(u * 32 + lane, v[u]);
+  } else {
+    for (int i0 = 0; i0 < count; i0 += 128) {
+      long long v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * 32 + lane;
+        v[u] = i < count ? load_index(src.tables, base + i, src.table64) : 0;
       }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * 32 + lane < count) put(i0 + u * 32 + lane, v[u]);
     }
   }
   __syncwarp();
@@ -88,7 +106,7 @@ __device__ __forceinline__ void table_window_refill(TableWindow& w, const PagedS
 // and return the token-validity mask (bit i = tile row i holds a real token).
 // Pages whose block id is outside [0, num_blocks) are not loaded and masked.
 // `row_pages` = pages of the row that hold tokens (never read past them).
-template <int D>
+template <int D, bool kWide = false>
 __device__ __forceinline__ void issue_kv_tile(const CUtensorMap* kmap, const CUtensorMap* vmap,
                                               const PagedSource& src, TableWindow& win, int row,
                                               int row_pages, int head, int tok0, int ntok,
@@ -101,7 +119,7 @@ __device__ __forceinline__ void issue_kv_tile(const CUtensorMap* kmap, const CUt
   const int first_page = tok0 / src.block_size;
   const int last_page = (tok0 + ntok - 1) / src.block_size;
   if (win.row != row || first_page < win.first || last_page >= win.first + win.count)
-    table_window_refill(win, src, row, first_page, row_pages, err, lane);
+    table_window_refill<kWide>(win, src, row, first_page, row_pages, err, lane);
   uint32_t mlo = 0, mhi = 0, nvalid = 0;
   for (int j0 = 0; j0 < boxes; j0 += 32) {
     const int j = j0 + lane;
@@ -153,6 +171,7 @@ __device__ __forceinline__ void issue_kv_tile(const CUtensorMap* kmap, const CUt
 // 128 bytes, row = head * tokens + token -- the layout issue_kv_tile produces
 // for one head and 64 tokens, so the consumers read both alike.  The validity
 // mask repeats the token bits once per head.
+template <bool kWide = false>
 __device__ __forceinline__ void issue_kv_tile_heads(const CUtensorMap* kmap, const CUtensorMap* vmap,
                                                     const PagedSource& src, TableWindow& win,
                                                     int row, int row_pages, int head0, int heads,
@@ -162,7 +181,7 @@ __device__ __forceinline__ void issue_kv_tile_heads(const CUtensorMap* kmap, con
   const int tokens = kKvTile / heads;
   const int page = tok0 / src.block_size;
   if (win.row != row || page < win.first || page >= win.first + win.count)
-    table_window_refill(win, src, row, page, row_pages, err, lane);
+    table_window_refill<kWide>(win, src, row, page, row_pages, err, lane);
   if (lane == 0) {
     const int blk = win.ids[page - win.first];
     uint64_t m = 0;

@@ -589,11 +589,11 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       uint8_t* kdst = smem + s * L.stage_bytes;
       const int row_pages = (len + p.block_size - 1) / p.block_size;
       if (HB > 1)
-        issue_kv_tile_heads(&kmap, &vmap, src, win, cur.r, row_pages, cur.h * HB, HB, tok0, ntok,
+        issue_kv_tile_heads<true>(&kmap, &vmap, src, win, cur.r, row_pages, cur.h * HB, HB, tok0, ntok,
                             S::kTileBytes, kdst, kdst + S::kTileBytes, &full_bar[s],
                             &stage_mask[s], p.err, lane);
       else
-        issue_kv_tile<D>(&kmap, &vmap, src, win, cur.r, row_pages, cur.h, tok0, ntok, kdst,
+        issue_kv_tile<D, true>(&kmap, &vmap, src, win, cur.r, row_pages, cur.h, tok0, ntok, kdst,
                          kdst + S::kTileBytes, &full_bar[s], &stage_mask[s], p.err, lane);
       ++issued;
       cur.advance(len_s, B, HG, TT);
