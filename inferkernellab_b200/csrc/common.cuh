@@ -116,6 +116,26 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // -------------------------------------------------------------------- TMA
+// Hint: bring the 128-byte line holding `ptr` into L2.  No value is read, so it
+// is safe before griddepcontrol.wait (a later write by the previous kernel goes
+// to L2 and is what the real load after the wait returns).  `ptr` must point at
+// a byte of a live allocation.
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
+// L2 prefetch of the lines holding bytes [base, base + bytes) -- only lines that
+// contain at least one of those bytes -- by threads t, t + nthreads, ...
+__device__ __forceinline__ void prefetch_l2_span(const void* base, long long bytes, int t,
+                                                 int nthreads) {
+  if (bytes <= 0) return;
+  const uintptr_t first = reinterpret_cast<uintptr_t>(base) & ~static_cast<uintptr_t>(127);
+  const uintptr_t last = (reinterpret_cast<uintptr_t>(base) + bytes - 1) & ~static_cast<uintptr_t>(127);
+  for (uintptr_t a = first + static_cast<uintptr_t>(t) * 128; a <= last;
+       a += static_cast<uintptr_t>(nthreads) * 128)
+    prefetch_l2(reinterpret_cast<const void*>(a));
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

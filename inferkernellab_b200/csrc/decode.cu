@@ -463,6 +463,26 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
   }
+  // While the previous kernel may still run: L2 prefetch of the metadata that
+  // the prologue and the producer read first -- the lengths (CTA c takes lines
+  // c, c + grid, ...) and the block-table rows (CTA c takes rows c, c + grid,
+  // ...).  Between the layers of a model the weight stream evicts them from L2;
+  // this turns the first two dependent loads after the wait into L2 hits.
+  if (warp < kDecConsumerWarps) {
+    const int cw = kDecConsumerWarps * 32;
+    const long long lens_bytes = static_cast<long long>(B) * (p.lens64 ? 8 : 4);
+    const long long lens_lines = (lens_bytes + 127) / 128 + 1;  // base need not be aligned
+    for (long long ln = blockIdx.x; ln < lens_lines; ln += gridDim.x) {
+      const long long lo = ln * 128 - (reinterpret_cast<uintptr_t>(p.lens) & 127);
+      const long long s0 = lo < 0 ? 0 : lo;
+      const long long s1 = lo + 128 < lens_bytes ? lo + 128 : lens_bytes;
+      if (s1 > s0) prefetch_l2_span(static_cast<const char*>(p.lens) + s0, s1 - s0, tid, cw);
+    }
+    const int esz = p.table64 ? 8 : 4;
+    for (int r = blockIdx.x; r < B; r += gridDim.x)
+      prefetch_l2_span(static_cast<const char*>(p.tables) + static_cast<long long>(r) * p.table_stride * esz,
+                       static_cast<long long>(p.table_width) * esz, tid, cw);
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // The next kernel on the stream may be scheduled now; its CTAs run their own
   // set-up on SMs this grid leaves and then wait for it to complete.
