@@ -380,6 +380,10 @@ __device__ __forceinline__ void store4(typename E::T* dst, float4 v) {
 }
 
 constexpr int kMinTilesPerCta = 2;  // fewer split pieces on small problems
+// Problems with fewer tiles than this per CTA of the grid size their ranges to
+// the longest segment (see the range choice); bigger ones are cut into
+// grid-many equal ranges.
+constexpr int kAdaptMaxTiles = 32;
 // A segment of at most this many tiles is not split when the grid has a CTA
 // for every segment (see the range choice).
 constexpr int kSegWholeMaxTiles = 10;
@@ -478,10 +482,14 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       const long long s1 = lo + 128 < lens_bytes ? lo + 128 : lens_bytes;
       if (s1 > s0) prefetch_l2_span(static_cast<const char*>(p.lens) + s0, s1 - s0, tid, cw);
     }
+    // Only a table of at most 4 MiB: a table whose rows are far wider than the
+    // contexts (capacity for very long requests) would otherwise pull mostly
+    // unread bytes from DRAM.
     const int esz = p.table64 ? 8 : 4;
-    for (int r = blockIdx.x; r < B; r += gridDim.x)
-      prefetch_l2_span(static_cast<const char*>(p.tables) + static_cast<long long>(r) * p.table_stride * esz,
-                       static_cast<long long>(p.table_width) * esz, tid, cw);
+    if (static_cast<long long>(B) * p.table_width * esz <= (4ll << 20))
+      for (int r = blockIdx.x; r < B; r += gridDim.x)
+        prefetch_l2_span(static_cast<const char*>(p.tables) + static_cast<long long>(r) * p.table_stride * esz,
+                         static_cast<long long>(p.table_width) * esz, tid, cw);
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // The next kernel on the stream may be scheduled now; its CTAs run their own
@@ -507,8 +515,10 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
       acc += ((len_s[i] + TT - 1) / TT) * HG;
     }
     if (tid == 0) begin_s[B] = total_all;
-    // The longest segment, only where whole segments are possible at all.
-    if (decode_whole_segs_possible(B * HG, total_all, static_cast<int>(gridDim.x))) {
+    // The longest segment, only where whole segments are possible at all or
+    // the problem is small enough for the split size to depend on it.
+    if (decode_whole_segs_possible(B * HG, total_all, static_cast<int>(gridDim.x)) ||
+        total_all < static_cast<int>(gridDim.x) * kAdaptMaxTiles) {
       int most = 0;
       for (int i = lo; i < hi; ++i) most = max(most, (len_s[i] + TT - 1) / TT);
       if (most > 0) atomicMax(max_seg_tiles, most);
@@ -540,9 +550,20 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   const int total = begin_s[B];
   const bool whole_segs = decode_whole_segs_possible(B * HG, total, static_cast<int>(gridDim.x)) &&
                           *max_seg_tiles <= kSegWholeMaxTiles;
+  // Split size t (tiles per range).  A segment of n tiles cut into ranges of t
+  // is merged from ~n / t pieces, ~n / (t * kMergePB) dependent L2 round trips
+  // for the CTA that merges, against t tiles of streaming in every CTA; t ~
+  // sqrt(n * 1.4 / kMergePB) balances the two (1.4 ~ a loaded L2 round trip
+  // over one tile's streaming time, measured on B200: single long requests
+  // ran up to 40 % faster than with t = 2, configs 1-5 are unchanged).
+  constexpr int kMergePB = kTrans ? 16 / kElems4 : 4;  // pieces per merge round trip
+  int min_tiles = kMinTilesPerCta;
+  if (total < static_cast<int>(gridDim.x) * kAdaptMaxTiles)
+    min_tiles = max(min_tiles, static_cast<int>(sqrtf(static_cast<float>(*max_seg_tiles) *
+                                                       (1.4f / kMergePB))));
   const int ctas = whole_segs ? B * HG
                               : min(static_cast<int>(gridDim.x),
-                                    max(1, (total + kMinTilesPerCta - 1) / kMinTilesPerCta));
+                                    max(1, (total + min_tiles - 1) / min_tiles));
   if (static_cast<int>(blockIdx.x) >= ctas) return;
   int per_cta, my_begin, my_end;
   if (whole_segs) {

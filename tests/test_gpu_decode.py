@@ -69,18 +69,20 @@ def test_decode_matches_oracle(shape, dtype):
     assert_close(out, case.oracle(), dtype, str(shape))
 
 
-@pytest.mark.parametrize("hq,hkv,dim", [(32, 1, 128), (64, 1, 64), (32, 8, 128), (8, 2, 32),
-                                         (16, 16, 16)],
+@pytest.mark.parametrize("hq,hkv,dim,ctx", [(32, 1, 128, 32768), (64, 1, 64, 32768),
+                                             (32, 8, 128, 8192), (8, 2, 32, 8192),
+                                             (16, 16, 16, 8192)],
                          ids=["G32_D128", "G64_D64", "G4_D128", "G4_D32", "G1_D16"])
-def test_decode_long_request_merges_many_pieces(hq, hkv, dim):
-    """One 8192-token request: each segment is cut into ~64 split pieces, so the
-    merge runs many batches (transposed variants: lse and partial O loaded
-    together, 16 / outputs-per-thread pieces per batch) or, for G > 16, more
-    pieces than one 32-piece chunk of lse in shared memory."""
+def test_decode_long_request_merges_many_pieces(hq, hkv, dim, ctx):
+    """One long request: each segment is cut into ~20-45 split pieces (the split
+    size follows the longest segment), so the merge runs many batches
+    (transposed variants: lse and partial O loaded together, 16 / outputs-per-
+    thread pieces per batch) or, for G > 16 at 32768 tokens, more pieces than
+    one 32-piece chunk of lse in shared memory."""
     case = DecodeCase(batch=1, num_heads=hq, num_kv_heads=hkv, head_dim=dim, block_size=16,
-                      lens=[8192], dtype=torch.bfloat16, seed=hq * 131 + dim)
+                      lens=[ctx], dtype=torch.bfloat16, seed=hq * 131 + dim)
     out = paged_decode_attention(case.query, case.cache, case.tables, case.lens)
-    assert_close(out, case.oracle(), torch.bfloat16, f"Hq{hq} Hkv{hkv} D{dim}")
+    assert_close(out, case.oracle(), torch.bfloat16, f"Hq{hq} Hkv{hkv} D{dim} ctx{ctx}")
     assert check_device_errors() == 0
 
 
