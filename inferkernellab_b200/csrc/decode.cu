@@ -558,9 +558,14 @@ __global__ void __launch_bounds__(kDecThreads, kDecMinBlocks)
   // ran up to 40 % faster than with t = 2, configs 1-5 are unchanged).
   constexpr int kMergePB = kTrans ? 16 / kElems4 : 4;  // pieces per merge round trip
   int min_tiles = kMinTilesPerCta;
-  if (total < static_cast<int>(gridDim.x) * kAdaptMaxTiles)
-    min_tiles = max(min_tiles, static_cast<int>(sqrtf(static_cast<float>(*max_seg_tiles) *
-                                                       (1.4f / kMergePB))));
+  if (total < static_cast<int>(gridDim.x) * kAdaptMaxTiles) {
+    float t = sqrtf(static_cast<float>(*max_seg_tiles) * (1.4f / kMergePB));
+    // Heads-as-M: the nearest power of two, which divides the power-of-two
+    // segment lengths of uniform batches (t = 3 on 32-tile segments left more
+    // CTAs straddling two segments, each with two pieces to publish).
+    if constexpr (!kTrans) t = exp2f(rintf(log2f(fmaxf(t, 1.f))));
+    min_tiles = max(min_tiles, static_cast<int>(t));
+  }
   const int ctas = whole_segs ? B * HG
                               : min(static_cast<int>(gridDim.x),
                                     max(1, (total + min_tiles - 1) / min_tiles));
