@@ -5,14 +5,18 @@
 //   ceil(len_r / T) *tiles* of T = 64 / HB logical tokens x HB heads (64 K and
 //   64 V rows either way).  HB = 1 unless head-group tiles apply (below).  All
 //   segments are laid end to end (request major, then head group) and the
-//   resulting tile range is cut into gridDim.x
-//   equal contiguous pieces, one per CTA ("stream-K").  A CTA therefore walks
-//   whole segments plus at most one partial segment at each end, and every CTA
-//   moves the same number of K/V bytes whatever the context-length spread.
+//   resulting tile range is cut into equal contiguous pieces, one per CTA
+//   ("stream-K"): gridDim.x of them, or fewer on small problems, where the
+//   piece length follows the longest segment so that a long request is not
+//   split into more pieces than its merge can absorb; short segments that all
+//   fit the grid run unsplit, one CTA each.  A CTA therefore walks whole
+//   segments plus at most one partial segment at each end, and every CTA moves
+//   the same number of K/V bytes whatever the context-length spread.
 //   A segment covered by one CTA is written straight to `out`; a segment split
 //   over several CTAs writes a partial (normalised O and log-sum-exp) into the
 //   workspace, and the CTA that arrives last on the segment's counter merges the
-//   partials and resets the counter -- no second kernel, no spin waiting.
+//   partials in one pass (lse and O of several pieces per batch of loads) and
+//   resets the counter -- no second kernel, no spin waiting.
 //
 // Head-group tiles (HB = 2 or 4; head_dim 64/128, G * HB <= 16, T <= block
 // size): a tile is one TMA box per tensor -- T tokens of HB heads out of one
